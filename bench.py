@@ -1,0 +1,441 @@
+#!/usr/bin/env python
+"""Benchmark of the ovvs brute-force kNN path on B200.
+
+Workload (default, BASELINE.json metric "kNN queries/sec @ N=10M D=128 fp16 k=10"): config 3 --
+L2 kNN over N=10,000,000 x 128 fp16 rows drawn from a Gaussian mixture of 1,024 centres
+(centres ~ N(0, 4I), rows = centre + N(0, I)), Q=10,000 queries from the same mixture rounded to
+fp16, k=10, seed 2. Data is synthetic and generated on the GPU with torch's seeded CUDA RNG in
+1M-row chunks (chunk c uses seed 1000*seed + c), so every GPU count sees the same rows.
+
+One step = one search of all Q queries. `value` times K device-pointer searches
+(ovvsBruteForceSearchDevice, inputs resident in HBM) with CUDA events on the library's stream;
+`e2e` times K host-buffer searches through the C ABI (ovvsBruteForceSearch: pageable host
+queries in, host results out, copies inside the timed region). N>1 GPUs (torchrun): rows are
+sharded, every rank searches all queries, per-shard candidates meet in an NCCL all-gather;
+times are the max over ranks.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c3]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    "c1": dict(metric="l2", dtype="f32", n=100_000, dim=128, nq=1_000, k=10, dist="uniform",
+               seed=0, desc="L2 fp32, N=100k x 128 Uniform[0,1), Q=1000, k=10"),
+    "c2": dict(metric="inner_product", dtype="f32", n=1_000_000, dim=96, nq=10_000, k=100,
+               dist="unit", seed=1, desc="IP fp32, N=1M x 96 unit-norm N(0,1), Q=10k, k=100"),
+    "c3": dict(metric="l2", dtype="f16", n=10_000_000, dim=128, nq=10_000, k=10, dist="mixture",
+               centres=1024, centre_std=2.0, seed=2,
+               desc="L2 fp16, N=10M x 128 Gaussian mixture (1024 centres, var 4), Q=10k, k=10"),
+    "c5": dict(metric="inner_product", dtype="f16", n=100_000_000, dim=96, nq=100_000, k=100,
+               dist="unit", seed=4, desc="IP fp16, N=100M x 96 unit-norm, Q=100k, k=100"),
+}
+METRIC_NAME = "kNN queries/sec @ N=10M D=128 fp16 k=10 at 1/2/4/8 B200; % of roofline"
+CHUNK = 1_000_000
+
+
+# ---------------------------------------------------------------------------------------------
+# data
+# ---------------------------------------------------------------------------------------------
+def _gen_rows(cfg, start, stop, device, torch, queries=False):
+    """Rows [start, stop) of the dataset (or of the query set), as torch tensors on `device`."""
+    dim = cfg["dim"]
+    out = []
+    base_seed = cfg["seed"] * 1000 + (500 if queries else 0)
+    centres = None
+    if cfg["dist"] == "mixture":
+        g = torch.Generator(device=device).manual_seed(cfg["seed"] * 1000 + 999)
+        centres = torch.randn(cfg["centres"], dim, generator=g, device=device) * cfg["centre_std"]
+    for c in range(start // CHUNK, (stop + CHUNK - 1) // CHUNK):
+        lo, hi = max(start, c * CHUNK), min(stop, (c + 1) * CHUNK)
+        g = torch.Generator(device=device).manual_seed(base_seed + c)
+        rows = CHUNK
+        if cfg["dist"] == "uniform":
+            x = torch.rand(rows, dim, generator=g, device=device)
+        elif cfg["dist"] == "unit":
+            x = torch.randn(rows, dim, generator=g, device=device)
+            x = x / x.norm(dim=1, keepdim=True)
+        else:
+            lab = torch.randint(0, cfg["centres"], (rows,), generator=g, device=device)
+            x = centres[lab] + torch.randn(rows, dim, generator=g, device=device)
+        out.append(x[lo - c * CHUNK: hi - c * CHUNK])
+    x = torch.cat(out) if len(out) > 1 else out[0]
+    if cfg["dtype"] == "f16":
+        x = x.half()
+    return x.contiguous()
+
+
+def _queries(cfg, device, torch):
+    q = _gen_rows(cfg, 0, cfg["nq"], device, torch, queries=True)
+    return q.float().contiguous()  # fp16-rounded values for fp16 configs, passed as fp32
+
+
+# ---------------------------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.dev = device_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.dev)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = max(mx, float(parts[1]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[3:7]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p, "measured"
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, \
+            "fallback"
+
+
+def _traffic_from_profiles(config_name):
+    """DRAM bytes per fused-kernel launch from the committed ncu summary, scaled to the config."""
+    path = os.path.join(ROOT, "profiles", "knn_fused_traffic.txt")
+    try:
+        for line in open(path):
+            if line.startswith(f"{config_name} "):
+                return float(line.split()[1])
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------------------------
+# the reference CPU path (oracle/_ref/libovvs_ref.so, the reference built from its sources)
+# ---------------------------------------------------------------------------------------------
+def _reference_sample(cfg, data_host, q_host, threads, n_queries):
+    """Times the reference's FORCE_CPU ovvsBruteForceSearch on `n_queries` queries against all
+    rows: row shards of 1M, `threads` host threads per shard (one Resources each, sharing the
+    shard's immutable index as the reference allows). Returns (seconds, shard top-k results)."""
+    import ctypes
+
+    from oracle.cpu import DTYPES, METRICS, Reference
+
+    ref = Reference()
+    L = ref.lib
+    qs = np.ascontiguousarray(q_host[:n_queries], np.float32)
+    k = cfg["k"]
+    per = [np.array_split(np.arange(n_queries), threads)[t] for t in range(threads)]
+    res = [ref.resources() for _ in range(threads)]
+    total = 0.0
+    for s0 in range(0, cfg["n"], CHUNK):
+        shard = np.ascontiguousarray(data_host[s0: s0 + CHUNK])
+        ix = ctypes.c_void_p()
+        assert L.ovvsBruteForceBuildTyped(res[0], shard.ctypes.data_as(ctypes.c_void_p),
+                                          shard.shape[0], shard.shape[1], METRICS[cfg["metric"]],
+                                          DTYPES[cfg["dtype"]], ctypes.byref(ix)) == 0
+
+        def work(t):
+            idx = per[t]
+            if idx.size == 0:
+                return
+            qq = np.ascontiguousarray(qs[idx])
+            nb = np.empty(idx.size * k, np.int64)
+            ds = np.empty(idx.size * k, np.float32)
+            st = L.ovvsBruteForceSearch(res[t], ix, qq.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
+                                        idx.size, k, None,
+                                        nb.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)),
+                                        ds.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+            assert st == 0
+
+        th = [threading.Thread(target=work, args=(t,)) for t in range(threads)]
+        t0 = time.perf_counter()
+        for x in th:
+            x.start()
+        for x in th:
+            x.join()
+        total += time.perf_counter() - t0
+        L.ovvsBruteForceDestroy(ix)
+    for r in res:
+        L.ovvsResourcesDestroy(r)
+    return total
+
+
+def _reference_sizes(cfg, seconds):
+    threads = max(1, min(os.cpu_count() or 1, 64))
+    rate = 1.0e9  # reference naive fp32 GEMM, MAC/s per thread (measured ~1.06e9 on C1)
+    nq = int(seconds * rate * threads / (cfg["n"] * cfg["dim"]))
+    nq = max(threads, min(cfg["nq"], nq // threads * threads))
+    return threads, nq
+
+
+def run_reference_arm(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import torch
+
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    data = _gen_rows(cfg, 0, cfg["n"], dev, torch)
+    data_host = data.cpu().numpy()
+    if cfg["dtype"] == "f16":
+        data_host = data_host.view(np.float16)
+    q_host = _queries(cfg, dev, torch).cpu().numpy()
+    del data
+    threads, nq = _reference_sizes(cfg, args.ref_seconds)
+    for _ in range(args.warmup):
+        _reference_sample(cfg, data_host, q_host, threads, threads)
+    secs = [_reference_sample(cfg, data_host, q_host, threads, nq) for _ in range(args.steps)]
+    t = sum(secs)
+    value = nq * args.steps / t
+    line = {
+        "metric": METRIC_NAME, "value": value, "unit": "queries/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": f"{args.config}: {cfg['desc']}",
+                   "sample": f"{nq} of {cfg['nq']} queries x all {cfg['n']} rows per step"},
+        "cpu_baseline": {"value": value, "unit": "queries/s", "cores": threads,
+                         "kind": "reference",
+                         "sample": f"{nq} queries x {cfg['n']} rows (1M-row shards, {threads} "
+                                   "threads with one Resources each, FORCE_CPU)"},
+        "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------------
+def run_ours(args, cfg):
+    import torch
+    import torch.distributed as dist
+
+    import ovvs_b200 as ov
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+        uid = [ov.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        res = ov.Resources.sharded(local, rank, world, uid[0])
+    else:
+        res = ov.Resources.sharded(local, 0, 1, None)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    n, dim, nq, k = cfg["n"], cfg["dim"], cfg["nq"], cfg["k"]
+    lo, hi = rank * n // world, (rank + 1) * n // world
+    shard = _gen_rows(cfg, lo, hi, dev, torch)
+    shard_host = shard.cpu().numpy()
+    if cfg["dtype"] == "f16":
+        shard_host = shard_host.view(np.float16)
+    del shard
+    t0 = time.perf_counter()
+    ix = ov.BruteIndex.build(shard_host, metric=cfg["metric"], dtype=cfg["dtype"], resources=res,
+                             row_offset=lo if world > 1 else None)
+    build_s = time.perf_counter() - t0
+    dq = _queries(cfg, dev, torch)
+    q_host = dq.cpu().numpy()
+    k_eff = min(k, n)
+    dn = torch.empty((nq, k_eff), dtype=torch.int64, device=dev)
+    dd = torch.empty((nq, k_eff), dtype=torch.float32, device=dev)
+    stream = torch.cuda.ExternalStream(res.stream(), device=dev)
+    torch.cuda.synchronize()
+
+    # warm-up (also grows the workspaces)
+    for _ in range(args.warmup):
+        ix.search_device(dq, k, dn, dd)
+    res.synchronize()
+
+    # ---- device-resident timing, phase events per launch --------------------------------
+    res.set_profiling(True)
+    phases = []
+    barrier()
+    with ClockSampler(local) as clocks:
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            ix.search_device(dq, k, dn, dd)
+            phases.append(res.last_phase_ms())
+        ev1.record(stream)
+        ev1.synchronize()
+        res.synchronize()
+        barrier()
+    res.set_profiling(False)
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    ms_step = ms / args.steps
+    value = nq / (ms_step / 1e3)
+
+    # ---- end to end through the C ABI with host buffers --------------------------------
+    nb_h = np.empty(nq * k, np.int64)
+    ds_h = np.empty(nq * k, np.float32)
+    for _ in range(max(1, args.warmup)):
+        ix.search(q_host, k=k, out=(nb_h, ds_h))
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        ix.search(q_host, k=k, out=(nb_h, ds_h))
+    e1.record(stream)
+    e1.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+    # results must agree between the two paths
+    assert np.array_equal(nb_h[: nq * k_eff].reshape(nq, k_eff), dn.cpu().numpy())
+
+    fused_ms = statistics.mean(p[1] for p in phases)
+    peaks, peak_kind = _peaks()
+    flops = 2.0 * nq * (hi - lo) * dim
+    achieved = flops / (fused_ms / 1e3) / 1e12
+    peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+    traffic = _traffic_from_profiles(args.config)
+    clk = clocks.summary()
+
+    line = None
+    if rank == 0:
+        line = {
+            "metric": METRIC_NAME, "value": value, "unit": "queries/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f16" if cfg["dtype"] == "f16" else "f32", "data": "synthetic",
+            "config": {
+                "workload": f"{args.config}: {cfg['desc']}", "n": n, "dim": dim, "nq": nq, "k": k,
+                "metric": cfg["metric"], "rows_per_gpu": hi - lo,
+                "parallelism": f"rows sharded over {world} GPU(s), NCCL all-gather merge"
+                if world > 1 else "1 GPU",
+                "l2": "inputs larger than L2 (database >> 126 MB), no flush needed",
+                "build_s": round(build_s, 3),
+                "phase_ms_mean": [round(statistics.mean(p[i] for p in phases), 4)
+                                  for i in range(4)],
+            },
+            "e2e": {"value": nq / (e2e_ms / 1e3), "unit": "queries/s",
+                    "h2d_bytes_per_step": nq * dim * 4, "d2h_bytes_per_step": nq * k_eff * 12},
+            "gpu_launches": args.steps * (3 if world == 1 else 4),
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+                         "kernel": "knn_fused_kernel", "flops_per_launch": flops,
+                         "peak_source": f"{peak_kind} bf16 dense sustained (fp16 MMA rate)"},
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"],
+                       "reasons": clk["reasons"]},
+        }
+    ix.close()
+    if world > 1:
+        dist.barrier()
+    res.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads, nq_s = _reference_sizes(cfg, args.ref_seconds)
+        data_host = shard_host
+        secs = _reference_sample(cfg, data_host, q_host, threads, nq_s)
+        line["cpu_baseline"] = {
+            "value": nq_s / secs, "unit": "queries/s", "cores": threads, "kind": "reference",
+            "sample": f"{nq_s} queries x all {n} rows: the reference library built from its "
+                      f"sources (oracle/_ref), FORCE_CPU, 1M-row shards, {threads} threads"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c3")
+    ap.add_argument("--ref-seconds", type=float, default=12.0,
+                    help="target seconds of reference CPU work per sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        print("note: warm-up raised to 3", file=sys.stderr)
+        args.warmup = 3
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        return run_reference_arm(args, cfg)
+    return run_ours(args, cfg)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

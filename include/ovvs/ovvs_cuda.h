@@ -1,0 +1,84 @@
+#pragma once
+
+/* B200 extensions to the ovvs C ABI.
+ *
+ * None of these entry points has a counterpart in the reference (its ABI is single-process,
+ * host-pointer only). They exist for two kinds of caller:
+ *   - callers whose queries and results already live in GPU memory (device-pointer search), and
+ *   - one-process-per-GPU deployments that shard the database rows across GPUs and merge the
+ *     per-shard candidates with an NCCL all-gather.
+ * Everything here uses the same handles and status codes as ovvs.h. */
+
+#include "ovvs.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- streams and errors ------------------------------------------------------------------ */
+
+/* The cudaStream_t (as void*) that this Resources enqueues its work on. Created on first use. */
+OVVS_API ovvsStatus ovvsResourcesStream(ovvsResources_t res, void** stream);
+
+/* Waits for all work enqueued through this Resources and reports what the kernels recorded:
+   OVVS_STATUS_ERROR if a kernel's bounded wait gave up (its watchdog), or a CUDA error. */
+OVVS_API ovvsStatus ovvsResourcesSynchronize(ovvsResources_t res);
+
+/* CUDA device ordinal this Resources is bound to. */
+OVVS_API ovvsStatus ovvsResourcesDevice(ovvsResources_t res, int32_t* device);
+
+/* Per-phase device timing. When enabled, each search records CUDA events on the Resources'
+   stream at its phase boundaries; ovvsResourcesLastPhaseMs waits for the last search and writes
+   up to `count` durations in milliseconds: [0] query preparation (+ allow bits), [1] fused
+   distance / top-k kernel, [2] candidate merge + exact re-rank, [3] cross-shard all-gather and
+   merge (0 on one GPU). */
+OVVS_API ovvsStatus ovvsResourcesSetProfiling(ovvsResources_t res, int32_t enable);
+OVVS_API ovvsStatus ovvsResourcesLastPhaseMs(ovvsResources_t res, float* ms, int32_t count);
+
+/* ---- device-pointer search ---------------------------------------------------------------- */
+
+/* Same contract as ovvsBruteForceSearch, but queries, bitset, neighbors and distances are device
+   pointers on the Resources' device, and the call only enqueues work on the Resources' stream
+   (no host synchronisation). Output rows have stride min(k, n). Call ovvsResourcesSynchronize
+   (or synchronise the stream) before reading the results. On a sharded Resources the call is
+   collective: every rank passes the same queries and receives the global result. */
+OVVS_API ovvsStatus ovvsBruteForceSearchDevice(ovvsResources_t res, ovvsBruteForceIndex_t index,
+                                               const float* d_queries, int64_t nq, int64_t k,
+                                               const uint8_t* d_bitset, int64_t* d_neighbors,
+                                               float* d_distances);
+
+/* ---- one process per GPU ------------------------------------------------------------------ */
+
+/* Size in bytes of the NCCL unique id that ovvsNcclUniqueId writes (128). */
+OVVS_API int32_t ovvsNcclUniqueIdSize(void);
+
+/* Rank 0 calls this once and shares the bytes with every other rank (any transport). */
+OVVS_API ovvsStatus ovvsNcclUniqueId(uint8_t* id, int32_t len);
+
+/* Creates a Resources bound to CUDA device `device` that is rank `rank` of `world` ranks. With
+   world > 1 it owns an NCCL communicator built from `nccl_id` (collective: all ranks must call).
+   Searches and k-means fits through it are collective over the ranks. */
+OVVS_API ovvsStatus ovvsResourcesCreateSharded(ovvsResources_t* res, int32_t device,
+                                               int32_t rank, int32_t world,
+                                               const uint8_t* nccl_id, int32_t len);
+
+/* Builds this rank's shard: `n_local` rows that are rows [row_offset, row_offset + n_local) of
+   the global dataset. Search results report global row ids, and a search bitset is indexed by
+   global row id. */
+OVVS_API ovvsStatus ovvsBruteForceBuildShard(ovvsResources_t res, const void* dataset,
+                                             int64_t n_local, int64_t dim, ovvsMetric metric,
+                                             ovvsDType dtype, int64_t row_offset,
+                                             ovvsBruteForceIndex_t* index);
+
+/* Collective k-means over row shards: rank r passes rows [row_offset, row_offset + n_local) of a
+   dataset with n_total rows. Seeding picks the same global rows as ovvsKMeansFit would on the
+   whole dataset; per-iteration sums and counts are all-reduced, so every rank ends with the same
+   centroids. */
+OVVS_API ovvsStatus ovvsKMeansFitShard(ovvsResources_t res, const float* dataset, int64_t n_local,
+                                       int64_t row_offset, int64_t n_total, int64_t dim,
+                                       int32_t nclusters, int32_t iters,
+                                       ovvsKMeansModel_t* model);
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,372 @@
+/* CPU restatement of the reference's brute-force kNN / k-means arithmetic.
+ *
+ * TEST INFRASTRUCTURE ONLY (see ovvs_oracle.h): used by tests/ and by bench.py's CPU-baseline
+ * leg as the checker, never by the product library. Compiled with -ffp-contract=off so that
+ * every multiply and add rounds separately, like the reference's scalar loops on x86-64.
+ *
+ * Citations are file:line in the reference repository (manan-ramnani/ovVS 0.2.0). */
+
+#include "ovvs_oracle.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <limits>
+#include <numeric>
+#include <random>
+#include <thread>
+#include <vector>
+
+namespace {
+
+constexpr int32_t kL2 = 0, kL2Sqrt = 1, kIP = 2, kCos = 3, kHamming = 4, kLp = 5;
+
+/* internal.hpp:215-225: sequential dot product and squared norm. */
+float dot_seq(const float* a, const float* b, int64_t d) {
+  float s = 0.f;
+  for (int64_t i = 0; i < d; ++i) s += a[i] * b[i];
+  return s;
+}
+float nrm2sq_seq(const float* a, int64_t d) {
+  float s = 0.f;
+  for (int64_t i = 0; i < d; ++i) s += a[i] * a[i];
+  return s;
+}
+/* internal.hpp:57-64. */
+float l2sq_seq(const float* a, const float* b, int64_t d) {
+  float s = 0.f;
+  for (int64_t i = 0; i < d; ++i) {
+    const float t = a[i] - b[i];
+    s += t * t;
+  }
+  return s;
+}
+
+/* internal.hpp:240-272 distance_one: the non-expanded metrics. */
+float distance_direct(int32_t metric, const float* x, const float* y, int64_t d, float arg) {
+  switch (metric) {
+    case kL2:
+      return l2sq_seq(x, y, d);
+    case kL2Sqrt:
+      return std::sqrt(l2sq_seq(x, y, d));
+    case kIP:
+      return -dot_seq(x, y, d);
+    case kCos: {
+      const float nx = std::sqrt(std::max(nrm2sq_seq(x, d), 1e-12f));
+      const float ny = std::sqrt(std::max(nrm2sq_seq(y, d), 1e-12f));
+      return 1.f - dot_seq(x, y, d) / (nx * ny);
+    }
+    case kHamming: {
+      int s = 0;
+      for (int64_t i = 0; i < d; ++i) {
+        const uint32_t ax = static_cast<uint32_t>(x[i] >= 0.f);
+        const uint32_t ay = static_cast<uint32_t>(y[i] >= 0.f);
+        s += static_cast<int>(ax ^ ay);
+      }
+      return static_cast<float>(s);
+    }
+    case kLp: {
+      const float p = arg > 0.f ? arg : 2.f;
+      float s = 0.f;
+      for (int64_t i = 0; i < d; ++i) s += std::pow(std::fabs(x[i] - y[i]), p);
+      return std::pow(s, 1.f / p);
+    }
+    default:
+      return l2sq_seq(x, y, d);
+  }
+}
+
+bool expanded(int32_t metric) { return metric == kL2 || metric == kIP || metric == kCos; }
+
+/* cpu_prims.cpp:24-32 topk_before: numbers before NaN, direction, then lower ordinal. */
+inline bool before(float a, int64_t ia, float b, int64_t ib, bool largest) {
+  if (a < b) return !largest;
+  if (a > b) return largest;
+  const bool an = std::isnan(a), bn = std::isnan(b);
+  if (an != bn) return !an;
+  return ia < ib;
+}
+
+/* cpu_prims.cpp:61-106. The heap (k <= 64) and partial_sort (k > 64) branches both produce the
+   first k elements of the total order, so one selection routine covers both. */
+void topk_rows(const float* scores, int64_t rows, int64_t cols, int64_t k, int64_t* indices,
+               float* values, bool largest) {
+  if (rows <= 0 || cols <= 0 || k <= 0) return;
+  k = std::min(k, cols);
+  std::vector<int64_t> idx(static_cast<size_t>(cols));
+  for (int64_t r = 0; r < rows; ++r) {
+    const float* row = scores + r * cols;
+    std::iota(idx.begin(), idx.end(), 0);
+    std::partial_sort(idx.begin(), idx.begin() + k, idx.end(),
+                      [&](int64_t i, int64_t j) { return before(row[i], i, row[j], j, largest); });
+    for (int64_t t = 0; t < k; ++t) {
+      indices[r * k + t] = idx[static_cast<size_t>(t)];
+      values[r * k + t] = row[idx[static_cast<size_t>(t)]];
+    }
+  }
+}
+
+/* mixer.cpp:174-221 for a block of queries against all rows; ynorm precomputed. */
+void pairwise_block(int32_t metric, const float* x, int64_t nx, const float* y, int64_t ny,
+                    int64_t dim, const float* ynorm, float* out, float arg) {
+  if (!expanded(metric)) {
+    for (int64_t i = 0; i < nx; ++i)
+      for (int64_t j = 0; j < ny; ++j)
+        out[i * ny + j] = distance_direct(metric, x + i * dim, y + j * dim, dim, arg);
+    return;
+  }
+  for (int64_t i = 0; i < nx; ++i) {
+    const float* xi = x + i * dim;
+    const float xn = nrm2sq_seq(xi, dim);
+    for (int64_t j = 0; j < ny; ++j) {
+      /* cpu_prims.cpp:48-58 naive GEMM (trans_b): sequential fp32 accumulation. */
+      const float ip = dot_seq(xi, y + j * dim, dim);
+      float v;
+      if (metric == kIP) {
+        v = -ip;
+      } else if (metric == kCos) {
+        const float nxv = std::sqrt(std::max(xn, 1e-12f));
+        const float nyv = std::sqrt(std::max(ynorm[j], 1e-12f));
+        v = 1.f - ip / (nxv * nyv);
+      } else {
+        v = xn + ynorm[j] - 2.f * ip;
+      }
+      out[i * ny + j] = v;
+    }
+  }
+}
+
+template <class F>
+void parallel_for(int64_t n, int32_t nthreads, F&& fn) {
+  if (nthreads <= 1 || n <= 1) {
+    fn(int64_t{0}, n);
+    return;
+  }
+  const int64_t t = std::min<int64_t>(nthreads, n);
+  std::vector<std::thread> th;
+  for (int64_t i = 0; i < t; ++i) {
+    const int64_t b = n * i / t, e = n * (i + 1) / t;
+    th.emplace_back([&fn, b, e] { fn(b, e); });
+  }
+  for (auto& x : th) x.join();
+}
+
+}  // namespace
+
+extern "C" {
+
+float oracle_f16_to_f32(uint16_t h) {
+  /* internal.hpp:804-829 */
+  const uint32_t sign = (static_cast<uint32_t>(h & 0x8000u) << 16);
+  const uint32_t exp = (h >> 10) & 0x1fu;
+  uint32_t man = h & 0x3ffu;
+  uint32_t bits;
+  if (exp == 0) {
+    if (man == 0) {
+      bits = sign;
+    } else {
+      int32_t e = 127 - 15 + 1;
+      while ((man & 0x400u) == 0) {
+        man <<= 1;
+        --e;
+      }
+      man &= 0x3ffu;
+      bits = sign | (static_cast<uint32_t>(e) << 23) | (man << 13);
+    }
+  } else if (exp == 31) {
+    bits = sign | 0x7f800000u | (man << 13);
+  } else {
+    bits = sign | ((exp + (127 - 15)) << 23) | (man << 13);
+  }
+  float f;
+  std::memcpy(&f, &bits, sizeof(f));
+  return f;
+}
+
+uint16_t oracle_f32_to_f16_trunc(float f) {
+  /* internal.hpp:831-840: exponent clamp, mantissa truncated, subnormals flushed to signed 0. */
+  uint32_t bits = 0;
+  std::memcpy(&bits, &f, sizeof(bits));
+  const uint32_t sign = (bits >> 16) & 0x8000u;
+  const int32_t exp = static_cast<int32_t>((bits >> 23) & 0xffu) - 127 + 15;
+  const uint32_t man = bits & 0x7fffffu;
+  if (exp <= 0) return static_cast<uint16_t>(sign);
+  if (exp >= 31) return static_cast<uint16_t>(sign | 0x7c00u);
+  return static_cast<uint16_t>(sign | (static_cast<uint32_t>(exp) << 10) | (man >> 13));
+}
+
+uint16_t oracle_f32_to_f16_rne(float value) {
+  /* internal.hpp:83-106 */
+  uint32_t f;
+  std::memcpy(&f, &value, sizeof(f));
+  const uint16_t sign = static_cast<uint16_t>((f >> 16) & 0x8000u);
+  const uint32_t a = f & 0x7FFFFFFFu;
+  if (a > 0x7F800000u) return static_cast<uint16_t>(sign | 0x7E00u);
+  if (a >= 0x47800000u) return static_cast<uint16_t>(sign | 0x7C00u);
+  if (a >= 0x38800000u) {
+    const uint32_t mant = a & 0x7FFFFFu;
+    const uint32_t e = (a >> 23) - 112u;
+    uint32_t half = (e << 10) | (mant >> 13);
+    const uint32_t rest = mant & 0x1FFFu;
+    if (rest > 0x1000u || (rest == 0x1000u && (half & 1u))) ++half;
+    return static_cast<uint16_t>(sign | half);
+  }
+  if (a <= 0x33000000u) return sign;
+  const uint32_t mant = (a & 0x7FFFFFu) | 0x800000u;
+  const uint32_t shift = 126u - (a >> 23);
+  uint32_t half = mant >> shift;
+  const uint32_t rest = mant & ((1u << shift) - 1u);
+  const uint32_t halfway = 1u << (shift - 1u);
+  if (rest > halfway || (rest == halfway && (half & 1u))) ++half;
+  return static_cast<uint16_t>(sign | half);
+}
+
+void oracle_convert_to_f32(int32_t dtype, const void* src, int64_t n, int64_t dim, float* out) {
+  const int64_t cells = n * dim;
+  if (dtype == 0) {
+    std::memcpy(out, src, static_cast<size_t>(cells) * sizeof(float));
+  } else if (dtype == 1) {
+    const auto* h = static_cast<const uint16_t*>(src);
+    for (int64_t i = 0; i < cells; ++i) out[i] = oracle_f16_to_f32(h[i]);
+  } else if (dtype == 2) {
+    const auto* p = static_cast<const int8_t*>(src);
+    for (int64_t i = 0; i < cells; ++i) out[i] = static_cast<float>(p[i]);
+  } else {
+    const auto* p = static_cast<const uint8_t*>(src);
+    for (int64_t i = 0; i < cells; ++i) out[i] = static_cast<float>(p[i]);
+  }
+}
+
+void oracle_pairwise(int32_t metric, const float* x, int64_t nx, const float* y, int64_t ny,
+                     int64_t dim, float* out, float metric_arg) {
+  std::vector<float> ynorm(static_cast<size_t>(ny));
+  for (int64_t j = 0; j < ny; ++j) ynorm[static_cast<size_t>(j)] = nrm2sq_seq(y + j * dim, dim);
+  pairwise_block(metric, x, nx, y, ny, dim, ynorm.data(), out, metric_arg);
+}
+
+void oracle_topk(const float* scores, int64_t rows, int64_t cols, int64_t k, int64_t* indices,
+                 float* values, int32_t largest) {
+  topk_rows(scores, rows, cols, k, indices, values, largest != 0);
+}
+
+void oracle_brute_search(const float* data, int64_t n, int64_t dim, int32_t metric,
+                         const float* queries, int64_t nq, int64_t k, const uint8_t* bitset,
+                         int64_t* neighbors, float* distances, int32_t nthreads) {
+  std::vector<float> ynorm(static_cast<size_t>(n));
+  for (int64_t j = 0; j < n; ++j) ynorm[static_cast<size_t>(j)] = nrm2sq_seq(data + j * dim, dim);
+  const int64_t k_eff = std::min(k, n);
+  const float inf = std::numeric_limits<float>::infinity();
+  parallel_for(nq, nthreads, [&](int64_t q0, int64_t q1) {
+    const int64_t block = 16;
+    std::vector<float> scores(static_cast<size_t>(block * n));
+    for (int64_t b = q0; b < q1; b += block) {
+      const int64_t m = std::min(block, q1 - b);
+      /* metric_arg 2.f: mixer.cpp:847 */
+      pairwise_block(metric, queries + b * dim, m, data, n, dim, ynorm.data(), scores.data(), 2.f);
+      if (bitset) {
+        /* mixer.cpp:849-857 + internal.hpp:274-277 (LSB-first) */
+        for (int64_t i = 0; i < m; ++i)
+          for (int64_t j = 0; j < n; ++j)
+            if (!((bitset[j >> 3] >> (j & 7)) & 1u)) scores[static_cast<size_t>(i * n + j)] = inf;
+      }
+      topk_rows(scores.data(), m, n, k, neighbors + b * k_eff, distances + b * k_eff, false);
+    }
+  });
+  /* mixer.cpp:860-862: negation covers nq*k entries (k as requested, not min(k, n)). */
+  if (metric == kIP)
+    for (int64_t i = 0; i < nq * k; ++i) distances[i] = -distances[i];
+}
+
+int32_t oracle_kmeans_init_rows(int64_t n, int32_t k, int64_t* rows) {
+  /* mixer.cpp:879-890: std::mt19937(42), uniform_int_distribution<int64_t>(0, n-1), up to 8
+     redraws when the row was already used. */
+  if (n <= 0 || k <= 0) return -1;
+  k = std::max(1, std::min(k, static_cast<int32_t>(std::min<int64_t>(n, INT32_MAX))));
+  std::mt19937 rng(42u);
+  std::uniform_int_distribution<int64_t> pick(0, n - 1);
+  std::vector<int64_t> used;
+  for (int32_t c = 0; c < k; ++c) {
+    int64_t i = pick(rng);
+    for (int t = 0; t < 8 && std::find(used.begin(), used.end(), i) != used.end(); ++t)
+      i = pick(rng);
+    used.push_back(i);
+    rows[c] = i;
+  }
+  return k;
+}
+
+void oracle_kmeans_predict(const float* centroids, int32_t k, int64_t dim, const float* x,
+                           int64_t n, int64_t* labels, float* distances, int32_t nthreads) {
+  /* cluster.cpp:59-69: prim_pairwise(L2_EXPANDED) then prim_topk(k=1). */
+  std::vector<float> cnorm(static_cast<size_t>(k));
+  for (int32_t c = 0; c < k; ++c) cnorm[static_cast<size_t>(c)] = nrm2sq_seq(centroids + c * dim, dim);
+  parallel_for(n, nthreads, [&](int64_t b, int64_t e) {
+    std::vector<float> row(static_cast<size_t>(k));
+    for (int64_t i = b; i < e; ++i) {
+      pairwise_block(kL2, x + i * dim, 1, centroids, k, dim, cnorm.data(), row.data(), 2.f);
+      int64_t li;
+      float lv;
+      topk_rows(row.data(), 1, k, 1, &li, &lv, false);
+      labels[i] = li;
+      if (distances) distances[i] = lv;
+    }
+  });
+}
+
+void oracle_kmeans_step(const float* x, int64_t n, int64_t dim, int32_t k, float* centroids,
+                        int64_t* labels_out, float* dist_out, int32_t nthreads) {
+  std::vector<int64_t> labels(static_cast<size_t>(n));
+  std::vector<float> dist(static_cast<size_t>(n));
+  oracle_kmeans_predict(centroids, k, dim, x, n, labels.data(), dist.data(), nthreads);
+  /* mixer.cpp:902-918: serial fp32 sums in row order; centroid = sum * (1/cnt); empty clusters
+     keep the previous centroid. */
+  std::vector<float> sum(static_cast<size_t>(k) * static_cast<size_t>(dim), 0.f);
+  std::vector<int32_t> cnt(static_cast<size_t>(k), 0);
+  for (int64_t i = 0; i < n; ++i) {
+    const int64_t c = labels[static_cast<size_t>(i)];
+    if (c < 0 || c >= k) continue;
+    ++cnt[static_cast<size_t>(c)];
+    float* dst = sum.data() + c * dim;
+    const float* src = x + i * dim;
+    for (int64_t d = 0; d < dim; ++d) dst[d] += src[d];
+  }
+  for (int32_t c = 0; c < k; ++c) {
+    if (cnt[static_cast<size_t>(c)] == 0) continue;
+    float* dst = centroids + static_cast<size_t>(c) * dim;
+    const float* src = sum.data() + static_cast<size_t>(c) * dim;
+    const float inv = 1.f / static_cast<float>(cnt[static_cast<size_t>(c)]);
+    for (int64_t d = 0; d < dim; ++d) dst[d] = src[d] * inv;
+  }
+  if (labels_out) std::memcpy(labels_out, labels.data(), static_cast<size_t>(n) * sizeof(int64_t));
+  if (dist_out) std::memcpy(dist_out, dist.data(), static_cast<size_t>(n) * sizeof(float));
+}
+
+int32_t oracle_kmeans_fit(const float* x, int64_t n, int64_t dim, int32_t k, int32_t iters,
+                          float* centroids, int32_t nthreads) {
+  /* mixer.cpp:868-871 validation. */
+  if (!x || n <= 0 || dim <= 0 || k <= 0 || iters < 0 || n > INT32_MAX) return -1;
+  std::vector<int64_t> rows(static_cast<size_t>(k));
+  const int32_t keff = oracle_kmeans_init_rows(n, k, rows.data());
+  for (int32_t c = 0; c < keff; ++c)
+    std::memcpy(centroids + static_cast<size_t>(c) * dim, x + rows[static_cast<size_t>(c)] * dim,
+                static_cast<size_t>(dim) * sizeof(float));
+  for (int32_t it = 0; it < iters; ++it)
+    oracle_kmeans_step(x, n, dim, keff, centroids, nullptr, nullptr, nthreads);
+  return keff;
+}
+
+int32_t oracle_bitset_from_allow_list(int64_t n, const int64_t* ids, int64_t nids,
+                                      uint8_t* bitset) {
+  if (!bitset || n <= 0 || nids < 0) return 2;
+  const int64_t nbytes = (n + 7) / 8;
+  std::memset(bitset, 0, static_cast<size_t>(nbytes));
+  if (!ids || nids == 0) return 0;
+  for (int64_t i = 0; i < nids; ++i) {
+    const int64_t id = ids[i];
+    if (id < 0 || id >= n) continue;
+    bitset[id >> 3] = static_cast<uint8_t>(bitset[id >> 3] | (1u << (id & 7)));
+  }
+  return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,325 @@
+// Brute-force index build and search orchestration (see brute_force.hpp).
+#include "brute_force.hpp"
+
+#include <cub/device/device_radix_sort.cuh>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <limits>
+#include <vector>
+
+#include "../prim/prep.cuh"
+#include "../prim/select.cuh"
+
+namespace ovvs {
+namespace nb {
+namespace {
+
+using prim::kTileN;
+using prim::kTileQ;
+
+constexpr int kDTypeF32 = 0, kDTypeF16 = 1, kDTypeI8 = 2;
+constexpr int kItemOverheadTiles = 4;  // query-tile load + pipeline refill + list warm-up
+
+size_t elem_size(int dtype) {
+  if (dtype == kDTypeF32) return 4;
+  if (dtype == kDTypeF16) return 2;
+  return 1;  // I8, U8 and the byte-read F8/F4 types
+}
+
+// Splits dp (multiple of 16) into K chunks of 64 (SWIZZLE_128B), then 32 / 16 for the tail.
+void plan_chunks(int dp, int* nchunk, int* cx, int* cw) {
+  int n = 0, x = 0;
+  while (dp - x >= 64) {
+    cx[n] = x;
+    cw[n++] = 64;
+    x += 64;
+  }
+  if (dp - x >= 32) {
+    cx[n] = x;
+    cw[n++] = 32;
+    x += 32;
+  }
+  if (dp - x >= 16) {
+    cx[n] = x;
+    cw[n++] = 16;
+    x += 16;
+  }
+  *nchunk = n;
+}
+
+// Number of super-chunks per query tile: balances the per-CTA work of the statically strided
+// item schedule (every CTA runs items b, b + grid, ...) against the per-item overhead.
+int choose_num_sc(int num_qtiles, int num_dbtiles, int num_sms, int64_t cand_per_sc_bytes,
+                  int* tiles_per_item) {
+  int best_sc = 1, best_L = num_dbtiles;
+  double best = std::numeric_limits<double>::infinity();
+  const int max_sc = std::min(num_dbtiles, 512);
+  for (int sc = 1; sc <= max_sc; ++sc) {
+    const int L = (num_dbtiles + sc - 1) / sc;
+    const int sc_eff = (num_dbtiles + L - 1) / L;
+    if (sc_eff != sc) continue;
+    if (static_cast<double>(cand_per_sc_bytes) * sc > 1.5e9) break;
+    const int64_t items = static_cast<int64_t>(num_qtiles) * sc;
+    const int64_t grid = std::min<int64_t>(items, num_sms);
+    const int64_t waves = (items + grid - 1) / grid;
+    const double cost = static_cast<double>(waves) * (L + kItemOverheadTiles);
+    if (cost < best * 0.999) {
+      best = cost;
+      best_sc = sc;
+      best_L = L;
+    }
+  }
+  *tiles_per_item = best_L;
+  return best_sc;
+}
+
+}  // namespace
+
+int list_size_for(int64_t k_eff) {
+  const int64_t need = k_eff + std::max<int64_t>(2, (k_eff + 7) / 8);
+  for (int kl : {4, 8, 16, 32})
+    if (need <= kl) return kl;
+  return 0;
+}
+
+ovvsStatus build_from_device(rt::Resources& r, BruteIndex& ix, const void* d_data, int dtype,
+                             int64_t n, int64_t dim, int metric_raw, int64_t row_offset) {
+  if (n >= static_cast<int64_t>(keys::kEmptyId) || dim > 4096) return OVVS_STATUS_SHAPE_MISMATCH;
+  ix.device = r.device;
+  ix.sharded = false;
+  ix.n = n;
+  ix.n_total = n;
+  ix.row_offset = row_offset;
+  ix.dim = dim;
+  ix.metric_raw = metric_raw;
+  ix.metric = prim::normalize_metric(metric_raw);
+  ix.dtype = dtype;
+  ix.dp = static_cast<int>((dim + 15) / 16 * 16);
+  plan_chunks(ix.dp, &ix.nchunk, ix.chunk_x, ix.chunk_w);
+  if (ix.nchunk > prim::kMaxChunks) return OVVS_STATUS_UNSUPPORTED;
+  const bool hamming = ix.metric == prim::kMetricHamming;
+  ix.b_parts = (dtype == kDTypeF32 && !hamming) ? 2 : 1;
+  ix.n_pad = (n + kTileN - 1) / kTileN * kTileN;
+  ix.num_tiles = static_cast<int>(ix.n_pad / kTileN);
+  cudaStream_t s = r.stream;
+
+  rt::DeviceBuffer norm, key, ids, perm, keys_out, absmax, cub_tmp;
+  OVVS_TRY_CUDA(norm.reserve(n * sizeof(float)));
+  OVVS_TRY_CUDA(key.reserve(n * sizeof(float)));
+  OVVS_TRY_CUDA(ids.reserve(n * sizeof(uint32_t)));
+  OVVS_TRY_CUDA(perm.reserve(n * sizeof(uint32_t)));
+  OVVS_TRY_CUDA(keys_out.reserve(n * sizeof(float)));
+  OVVS_TRY_CUDA(absmax.reserve(sizeof(unsigned int)));
+  OVVS_TRY_CUDA(cudaMemsetAsync(absmax.get(), 0, sizeof(unsigned int), s));
+  prim::launch_row_stats(d_data, dtype, n, static_cast<int>(dim), ix.metric, norm.as<float>(),
+                         key.as<float>(), absmax.as<unsigned int>(), s);
+  OVVS_TRY_CUDA(cudaGetLastError());
+
+  ix.e_db = 0;
+  if (ix.b_parts == 2) {
+    unsigned int bits = 0;
+    OVVS_TRY_CUDA(cudaMemcpyAsync(&bits, absmax.get(), sizeof(bits), cudaMemcpyDeviceToHost, s));
+    OVVS_TRY_CUDA(cudaStreamSynchronize(s));
+    float mx;
+    std::memcpy(&mx, &bits, sizeof(mx));
+    if (mx > 0.f) ix.e_db = std::min(14 - std::ilogb(mx), 127);
+  }
+
+  // Stable sort of row ids by their ranking aux (radix sort keeps equal keys in id order, so
+  // identical rows stay in ascending id order).
+  {
+    std::vector<uint32_t> iota(static_cast<size_t>(n));
+    for (int64_t i = 0; i < n; ++i) iota[static_cast<size_t>(i)] = static_cast<uint32_t>(i);
+    OVVS_TRY_CUDA(cudaMemcpyAsync(ids.get(), iota.data(), n * sizeof(uint32_t),
+                                  cudaMemcpyHostToDevice, s));
+    size_t tmp_bytes = 0;
+    OVVS_TRY_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, tmp_bytes, key.as<float>(),
+                                                  keys_out.as<float>(), ids.as<uint32_t>(),
+                                                  perm.as<uint32_t>(), static_cast<int>(n), 0, 32,
+                                                  s));
+    OVVS_TRY_CUDA(cub_tmp.reserve(tmp_bytes + 16));
+    OVVS_TRY_CUDA(cub::DeviceRadixSort::SortPairs(cub_tmp.get(), tmp_bytes, key.as<float>(),
+                                                  keys_out.as<float>(), ids.as<uint32_t>(),
+                                                  perm.as<uint32_t>(), static_cast<int>(n), 0, 32,
+                                                  s));
+    OVVS_TRY_CUDA(cudaStreamSynchronize(s));  // iota must outlive the copy
+  }
+
+  const int stride = ix.b_parts * ix.dp;
+  OVVS_TRY_CUDA(ix.rows16.reserve(static_cast<size_t>(ix.n_pad) * stride * 2));
+  const bool keep_exact32 = dtype == kDTypeF32 && !hamming;
+  if (keep_exact32) OVVS_TRY_CUDA(ix.exact32.reserve(static_cast<size_t>(ix.n_pad) * dim * 4));
+  OVVS_TRY_CUDA(ix.aux.reserve(ix.n_pad * sizeof(float)));
+  OVVS_TRY_CUDA(ix.norm_sorted.reserve(ix.n_pad * sizeof(float)));
+  OVVS_TRY_CUDA(ix.row_id.reserve(ix.n_pad * sizeof(uint32_t)));
+  OVVS_TRY_CUDA(ix.inv_perm.reserve(n * sizeof(uint32_t)));
+  OVVS_TRY_CUDA(ix.tile_aux.reserve(ix.num_tiles * sizeof(float2)));
+  prim::launch_scatter_rows(d_data, dtype, n, ix.n_pad, static_cast<int>(dim), ix.dp, ix.b_parts,
+                            ix.metric, ix.e_db, perm.as<uint32_t>(), norm.as<float>(),
+                            key.as<float>(), ix.rows16.as<__half>(),
+                            keep_exact32 ? ix.exact32.as<float>() : nullptr, ix.aux.as<float>(),
+                            ix.norm_sorted.as<float>(), ix.row_id.as<uint32_t>(),
+                            ix.inv_perm.as<uint32_t>(), s);
+  OVVS_TRY_CUDA(cudaGetLastError());
+  prim::launch_tile_bounds(ix.aux.as<float>(), n, ix.num_tiles, ix.tile_aux.as<float2>(), s);
+  OVVS_TRY_CUDA(cudaGetLastError());
+  if (!keep_exact32) ix.exact32.release();
+
+  const uint64_t cols = static_cast<uint64_t>(stride);
+  if (!rt::encode_f16_2d(&ix.b64, ix.rows16.get(), cols, ix.n_pad, 64, kTileN) ||
+      !rt::encode_f16_2d(&ix.b32, ix.rows16.get(), cols, ix.n_pad, 32, kTileN) ||
+      !rt::encode_f16_2d(&ix.b16, ix.rows16.get(), cols, ix.n_pad, 16, kTileN)) {
+    return OVVS_STATUS_ERROR;
+  }
+  OVVS_TRY_CUDA(cudaStreamSynchronize(s));
+  return OVVS_STATUS_SUCCESS;
+}
+
+ovvsStatus build_from_host(rt::Resources& r, BruteIndex& ix, const void* data, int dtype,
+                           int64_t n, int64_t dim, int metric_raw, int64_t row_offset,
+                           bool sharded) {
+  const size_t bytes = static_cast<size_t>(n) * dim * elem_size(dtype);
+  rt::DeviceBuffer raw;
+  OVVS_TRY_CUDA(raw.reserve(bytes));
+  OVVS_TRY_CUDA(cudaMemcpyAsync(raw.get(), data, bytes, cudaMemcpyHostToDevice, r.stream));
+  ovvsStatus st = build_from_device(r, ix, raw.get(), dtype, n, dim, metric_raw, row_offset);
+  if (st != OVVS_STATUS_SUCCESS) return st;
+  ix.sharded = sharded && r.world > 1;
+  if (ix.sharded) {
+    int64_t total = n;
+    OVVS_TRY(rt::allreduce_i64_sum(r, &total));
+    ix.n_total = total;
+  }
+  return r.finish();
+}
+
+ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_queries, int64_t nq,
+                         int64_t k, const uint8_t* d_bitset, int64_t* d_neighbors,
+                         float* d_distances, int64_t* k_eff_out) {
+  cudaStream_t s = r.stream;
+  const int64_t k_eff = std::min<int64_t>(k, ix.n_total);
+  *k_eff_out = k_eff;
+  const int kl = list_size_for(k_eff);
+  if (kl == 0) return OVVS_STATUS_UNSUPPORTED;
+  if (ix.device != r.device) return OVVS_STATUS_INVALID_ARGUMENT;
+  const int64_t q_pad = (nq + kTileQ - 1) / kTileQ * kTileQ;
+  const int num_qtiles = static_cast<int>(q_pad / kTileQ);
+  const int dim = static_cast<int>(ix.dim);
+
+  r.mark(0);
+  __half* a16 = nullptr;
+  float *q_mul = nullptr, *xn = nullptr;
+  int* flag = nullptr;
+  OVVS_TRY(r.scratch(rt::kWsQueryA, static_cast<size_t>(q_pad) * 2 * ix.dp, &a16));
+  OVVS_TRY(r.scratch(rt::kWsQueryMul, q_pad, &q_mul));
+  OVVS_TRY(r.scratch(rt::kWsQueryNorm, q_pad, &xn));
+  OVVS_TRY(r.scratch(rt::kWsFlags, 4, &flag));
+  OVVS_TRY_CUDA(cudaMemsetAsync(flag, 0, sizeof(int), s));
+  prim::launch_query_prep(d_queries, nq, q_pad, dim, ix.dp, ix.metric, ix.e_db, a16, q_mul, xn,
+                          flag, s);
+  OVVS_TRY_CUDA(cudaGetLastError());
+
+  uint32_t* allow = nullptr;
+  if (d_bitset) {
+    OVVS_TRY(r.scratch(rt::kWsAllow, ix.n_pad / 32, &allow));
+    prim::launch_allow_bits(d_bitset, ix.row_offset, ix.row_id.as<uint32_t>(), ix.n, ix.n_pad,
+                            allow, s);
+    OVVS_TRY_CUDA(cudaGetLastError());
+  }
+
+  prim::FusedParams p{};
+  p.dp = ix.dp;
+  p.nchunk = ix.nchunk;
+  for (int c = 0; c < ix.nchunk; ++c) {
+    p.chunk_x[c] = ix.chunk_x[c];
+    p.chunk_w[c] = ix.chunk_w[c];
+  }
+  p.b_parts = ix.b_parts;
+  p.nunits = ix.b_parts * ix.nchunk;
+  if (!prim::plan_fused_smem(p, r.max_smem_optin)) return OVVS_STATUS_UNSUPPORTED;
+  p.query_split = ix.metric != prim::kMetricHamming;
+  p.q_lo_flag = flag;
+  p.num_qtiles = num_qtiles;
+  p.num_dbtiles = ix.num_tiles;
+  const int64_t cand_per_sc = q_pad * kl * static_cast<int64_t>(sizeof(uint64_t));
+  p.num_sc = choose_num_sc(num_qtiles, ix.num_tiles, r.num_sms, cand_per_sc, &p.tiles_per_item);
+  p.num_items = num_qtiles * p.num_sc;
+  p.n_rows = ix.n;
+  p.row_aux = ix.aux.as<float>();
+  p.tile_aux = ix.tile_aux.as<float2>();
+  p.row_id = ix.row_id.as<uint32_t>();
+  p.q_mul = q_mul;
+  p.allow = allow;
+  p.rank_kind = prim::rank_kind_of(ix.metric);
+  p.err = r.d_err;
+  uint64_t* cand = nullptr;
+  OVVS_TRY(r.scratch(rt::kWsCand, static_cast<size_t>(q_pad) * p.num_sc * kl, &cand));
+  p.out = cand;
+
+  prim::FusedMaps maps{};
+  const uint64_t a_cols = static_cast<uint64_t>(2 * ix.dp);
+  if (!rt::encode_f16_2d(&maps.a64, a16, a_cols, q_pad, 64, kTileQ) ||
+      !rt::encode_f16_2d(&maps.a32, a16, a_cols, q_pad, 32, kTileQ) ||
+      !rt::encode_f16_2d(&maps.a16, a16, a_cols, q_pad, 16, kTileQ)) {
+    return OVVS_STATUS_ERROR;
+  }
+  maps.b64 = ix.b64;
+  maps.b32 = ix.b32;
+  maps.b16 = ix.b16;
+  const int grid = static_cast<int>(std::min<int64_t>(p.num_items, r.num_sms));
+  r.mark(1);
+  OVVS_TRY_CUDA(prim::launch_knn_fused(maps, p, kl, grid, s));
+  r.mark(2);
+
+  prim::MergeParams m{};
+  m.cand = cand;
+  m.num_sc = p.num_sc;
+  m.kl = kl;
+  m.nq = nq;
+  m.dim = dim;
+  m.queries = d_queries;
+  m.xn = xn;
+  m.metric = ix.metric;
+  m.exact32 = ix.exact32.get() ? ix.exact32.as<float>() : nullptr;
+  m.rows16 = ix.rows16.as<__half>();
+  m.rows16_stride = ix.b_parts * ix.dp;
+  m.norm_sorted = ix.norm_sorted.as<float>();
+  m.inv_perm = ix.inv_perm.as<uint32_t>();
+  m.allow = allow;
+  m.row_offset = ix.row_offset;
+  m.k_eff = static_cast<int>(k_eff);
+  m.negate_output = ix.metric == prim::kMetricInnerProduct;
+  if (!ix.sharded) {
+    m.neighbors = d_neighbors;
+    m.distances = d_distances;
+    OVVS_TRY_CUDA(prim::launch_merge_rerank(m, s));
+    r.mark(3);
+    r.mark(4);
+    return OVVS_STATUS_SUCCESS;
+  }
+  // Sharded: exact per-shard top-k, all-gather over NVLink, then an exact (rank, id) merge.
+  const size_t cnt = static_cast<size_t>(nq) * k_eff;
+  float *srank = nullptr, *grank = nullptr;
+  int64_t *sgid = nullptr, *ggid = nullptr;
+  OVVS_TRY(r.scratch(rt::kWsShardRank, cnt, &srank));
+  OVVS_TRY(r.scratch(rt::kWsShardGid, cnt, &sgid));
+  OVVS_TRY(r.scratch(rt::kWsGatherRank, cnt * r.world, &grank));
+  OVVS_TRY(r.scratch(rt::kWsGatherGid, cnt * r.world, &ggid));
+  m.shard_rank = srank;
+  m.shard_gid = sgid;
+  OVVS_TRY_CUDA(prim::launch_merge_rerank(m, s));
+  r.mark(3);
+  OVVS_TRY(rt::status_of(ovvs::rt::nccl()->GroupStart()));
+  OVVS_TRY(rt::status_of(ovvs::rt::nccl()->AllGather(srank, grank, cnt, ncclFloat32, r.comm, s)));
+  OVVS_TRY(rt::status_of(ovvs::rt::nccl()->AllGather(sgid, ggid, cnt, ncclInt64, r.comm, s)));
+  OVVS_TRY(rt::status_of(ovvs::rt::nccl()->GroupEnd()));
+  OVVS_TRY_CUDA(prim::launch_shard_merge(grank, ggid, r.world, nq, static_cast<int>(k_eff),
+                                         m.negate_output, d_neighbors, d_distances, s));
+  r.mark(4);
+  return OVVS_STATUS_SUCCESS;
+}
+
+}  // namespace nb
+}  // namespace ovvs

@@ -1,0 +1,65 @@
+// Exact brute-force kNN index on one CUDA device (one shard of the rows when sharded).
+//
+// Reference: src/neighbors/indexes.cpp:9-25 (BruteIndex owns an fp32 copy), 236-268 (ABI),
+// src/prim/mixer.cpp:843-864 (brute_search_impl). Here the index owns, in HBM and in
+// norm-sorted row order ("positions"):
+//   rows16      [n_pad x b_parts*dp] fp16 tensor-core operand: the exact fp16 values (F16 / I8 /
+//               U8 datasets), sign vectors (Hamming), or a 2^e_db-scaled hi + lo split (F32);
+//   exact32     [n_pad x dim] fp32 original values (F32 datasets only) for exact re-ranking;
+//   aux         [n_pad] ranking addend / column scale; tile_aux [n_tiles] its per-tile range;
+//   norm_sorted [n_pad] reference nrm2sq of each row; row_id / inv_perm position <-> row id.
+// Padding rows (positions >= n) are zero and never selected.
+#pragma once
+
+#include <cstdint>
+
+#include "../prim/knn_fused.cuh"
+#include "../rt/runtime.hpp"
+
+namespace ovvs {
+namespace nb {
+
+struct BruteIndex {
+  int device = 0;
+  int64_t n = 0;          // rows in this shard
+  int64_t n_total = 0;    // rows over all shards (k is clamped to it)
+  int64_t row_offset = 0; // global id of local row 0
+  bool sharded = false;   // rows are one shard of a dataset spread over the Resources' ranks
+  int64_t dim = 0;
+  int metric_raw = 0;     // ovvsMetric as given
+  int metric = 0;         // prim::MetricCode
+  int dtype = 0;          // ovvsDType as given
+  int dp = 0;             // padded dim per part (multiple of 16)
+  int b_parts = 1;
+  int e_db = 0;           // power-of-two scale of the F32 split
+  int64_t n_pad = 0;
+  int num_tiles = 0;
+  int nchunk = 0;
+  int chunk_x[prim::kMaxChunks] = {};
+  int chunk_w[prim::kMaxChunks] = {};
+  rt::DeviceBuffer rows16, exact32, aux, tile_aux, norm_sorted, row_id, inv_perm;
+  CUtensorMap b64{}, b32{}, b16{};
+};
+
+// Builds (or rebuilds in place, reusing allocations) from rows already on the device.
+ovvsStatus build_from_device(rt::Resources& r, BruteIndex& ix, const void* d_data, int dtype,
+                             int64_t n, int64_t dim, int metric_raw, int64_t row_offset);
+
+// Builds from host rows (copied to the device). `sharded`: the rows are this rank's shard of a
+// dataset spread over r's ranks (collective: every rank calls it).
+ovvsStatus build_from_host(rt::Resources& r, BruteIndex& ix, const void* data, int dtype,
+                           int64_t n, int64_t dim, int metric_raw, int64_t row_offset,
+                           bool sharded);
+
+// Enqueues a search on r.stream. d_queries [nq x dim] fp32, d_bitset null or global-id bitset,
+// outputs [nq x k_eff] with k_eff = min(k, n_total) (written to *k_eff_out).
+ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_queries, int64_t nq,
+                         int64_t k, const uint8_t* d_bitset, int64_t* d_neighbors,
+                         float* d_distances, int64_t* k_eff_out);
+
+// Candidate-list size the fused kernel uses for k_eff results (k_eff plus a re-rank margin),
+// 0 when k_eff is larger than the register lists support.
+int list_size_for(int64_t k_eff);
+
+}  // namespace nb
+}  // namespace ovvs

@@ -1,0 +1,467 @@
+// Fused distance + top-k kernel. Design notes in knn_fused.cuh.
+#include "knn_fused.cuh"
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace ovvs {
+namespace prim {
+namespace {
+
+using keys::kEmptyKey;
+
+constexpr float kInf = __builtin_huge_valf();
+
+struct Smem {
+  uint8_t* base;
+  uint64_t* full;    // [nstages] TMA -> MMA
+  uint64_t* empty;   // [nstages] MMA -> TMA
+  uint64_t* tfull;   // [2] MMA -> epilogue
+  uint64_t* tempty;  // [2] epilogue -> MMA (4 arrivals: one per epilogue warp)
+  uint64_t* afull;   // query tile landed
+  uint64_t* aempty;  // MMA done with the query tile
+  uint64_t* drain;   // final MMA completion
+  uint32_t* tmem_slot;
+  volatile int* abort;
+};
+
+__device__ __forceinline__ Smem carve(const FusedParams& p, uint8_t* raw) {
+  Smem s;
+  s.base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s.base + p.bar_off);
+  s.full = bars;
+  s.empty = bars + p.nstages;
+  s.tfull = s.empty + p.nstages;
+  s.tempty = s.tfull + 2;
+  s.afull = s.tempty + 2;
+  s.aempty = s.afull + 1;
+  s.drain = s.aempty + 1;
+  s.tmem_slot = reinterpret_cast<uint32_t*>(s.drain + 1);
+  s.abort = reinterpret_cast<volatile int*>(s.tmem_slot + 1);
+  return s;
+}
+
+__device__ __forceinline__ const CUtensorMap* pick_map(int w, const CUtensorMap* m64,
+                                                       const CUtensorMap* m32,
+                                                       const CUtensorMap* m16) {
+  return w == 64 ? m64 : (w == 32 ? m32 : m16);
+}
+
+// Work item -> (query tile, super-chunk, tile range). Items are ordered super-chunk-major so
+// that CTAs running at the same time stream the same database tiles (L2 reuse).
+struct Item {
+  int qt, sc, t0, t1;
+};
+__device__ __forceinline__ Item item_of(const FusedParams& p, int item) {
+  Item it;
+  it.qt = item % p.num_qtiles;
+  it.sc = item / p.num_qtiles;
+  it.t0 = it.sc * p.tiles_per_item;
+  it.t1 = min(it.t0 + p.tiles_per_item, p.num_dbtiles);
+  return it;
+}
+
+// Bounded wait used only while unwinding: ignores the abort flag (the copies or MMAs it waits
+// for complete on their own), still gives up after the time limit.
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* err) {
+  if (ptx::mbar_try_wait(bar, parity)) return;
+  const uint64_t t0 = ptx::globaltimer();
+  while (!ptx::mbar_try_wait(bar, parity)) {
+    if (ptx::globaltimer() - t0 > ptx::kWaitLimitNs) {
+      atomicCAS(err, 0, kErrDrain);
+      return;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// TMA producer (one thread)
+// ------------------------------------------------------------------------------------------
+__device__ void run_producer(const FusedParams& p, const FusedMaps& maps, const Smem& s, bool lo) {
+  uint32_t unit = 0;
+  int a_loads = 0;
+  int cur_qt = -1;
+  bool ok = true;
+  for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
+    const Item it = item_of(p, item);
+    if (it.qt != cur_qt) {
+      if (a_loads > 0 &&
+          !ptx::mbar_wait(s.aempty, (a_loads - 1) & 1, s.abort, p.err, kErrWaitAEmpty)) {
+        ok = false;
+        break;
+      }
+      ptx::mbar_arrive_expect_tx(s.afull, p.a_tx_bytes[0] + (lo ? p.a_tx_bytes[1] : 0));
+      for (int part = 0; part < (lo ? 2 : 1); ++part) {
+        for (int c = 0; c < p.nchunk; ++c) {
+          const int w = p.chunk_w[c];
+          ptx::tma_load_2d(s.base + p.a_off[part][c], pick_map(w, &maps.a64, &maps.a32, &maps.a16),
+                           part * p.dp + p.chunk_x[c], it.qt * kTileQ, s.afull);
+        }
+      }
+      ++a_loads;
+      cur_qt = it.qt;
+    }
+    for (int t = it.t0; t < it.t1 && ok; ++t) {
+      for (int u = 0; u < p.nunits; ++u) {
+        const uint32_t slot = unit % p.nstages;
+        const uint32_t use = unit / p.nstages;
+        if (use > 0 &&
+            !ptx::mbar_wait(&s.empty[slot], (use - 1) & 1, s.abort, p.err, kErrWaitSlotEmpty)) {
+          ok = false;
+          break;
+        }
+        const int bp = u / p.nchunk, c = u % p.nchunk, w = p.chunk_w[c];
+        ptx::mbar_arrive_expect_tx(&s.full[slot], static_cast<uint32_t>(kTileN * w * 2));
+        ptx::tma_load_2d(s.base + p.stage_off + slot * kUnitBytes,
+                         pick_map(w, &maps.b64, &maps.b32, &maps.b16), bp * p.dp + p.chunk_x[c],
+                         t * kTileN, &s.full[slot]);
+        ++unit;
+      }
+    }
+  }
+  // Unwind: every load this thread issued must land before the CTA exits. The last load into
+  // each slot completes the phase (use & 1) of that slot's full barrier.
+  const uint32_t issued = unit;
+  for (uint32_t slot = 0; slot < static_cast<uint32_t>(p.nstages) && slot < issued; ++slot) {
+    const uint32_t last = ((issued - 1 - slot) / p.nstages) * p.nstages + slot;
+    drain_wait(&s.full[slot], (last / p.nstages) & 1, p.err);
+  }
+  if (a_loads > 0) drain_wait(s.afull, (a_loads - 1) & 1, p.err);
+}
+
+// ------------------------------------------------------------------------------------------
+// MMA issuer (one thread)
+// ------------------------------------------------------------------------------------------
+__device__ void run_mma(const FusedParams& p, const Smem& s, uint32_t tmem_base, bool lo) {
+  constexpr uint32_t kIdesc = ptx::idesc_f16_f32(kTileQ, kTileN);
+  const uint32_t base_addr = ptx::smem_addr(s.base);
+  uint32_t unit = 0, tile = 0;
+  int a_waits = 0, cur_qt = -1;
+  bool ok = true;
+  for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
+    const Item it = item_of(p, item);
+    if (it.qt != cur_qt) {
+      if (!ptx::mbar_wait(s.afull, a_waits & 1, s.abort, p.err, kErrWaitA)) {
+        ok = false;
+        break;
+      }
+      ++a_waits;
+      cur_qt = it.qt;
+      ptx::tc_fence_after();
+    }
+    for (int t = it.t0; t < it.t1 && ok; ++t) {
+      const uint32_t buf = tile & 1, use = tile >> 1;
+      if (use > 0 &&
+          !ptx::mbar_wait(&s.tempty[buf], (use - 1) & 1, s.abort, p.err, kErrWaitTmemEmpty)) {
+        ok = false;
+        break;
+      }
+      ptx::tc_fence_after();
+      const uint32_t d_tmem = tmem_base + buf * kTileN;
+      uint32_t acc = 0;
+      for (int u = 0; u < p.nunits; ++u) {
+        const uint32_t slot = unit % p.nstages;
+        const uint32_t suse = unit / p.nstages;
+        if (!ptx::mbar_wait(&s.full[slot], suse & 1, s.abort, p.err, kErrWaitSlotFull)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const int bp = u / p.nchunk, c = u % p.nchunk, w = p.chunk_w[c];
+        const uint32_t row_bytes = static_cast<uint32_t>(w * 2);
+        const uint32_t b_addr = base_addr + p.stage_off + slot * kUnitBytes;
+        const uint32_t a0 = base_addr + p.a_off[0][c];
+        const uint32_t a1 = base_addr + p.a_off[1][c];
+        for (int ks = 0; ks < w / 16; ++ks) {
+          const uint64_t bd = ptx::smem_desc(b_addr + ks * 32, row_bytes);
+          ptx::mma_f16_ss(d_tmem, ptx::smem_desc(a0 + ks * 32, row_bytes), bd, kIdesc, acc);
+          acc = 1;
+          if (bp == 0 && lo) {
+            ptx::mma_f16_ss(d_tmem, ptx::smem_desc(a1 + ks * 32, row_bytes), bd, kIdesc, 1);
+          }
+        }
+        ptx::mma_commit(&s.empty[slot]);  // slot reusable once these MMAs have read it
+        ++unit;
+      }
+      if (!ok) break;
+      ptx::mma_commit(&s.tfull[buf]);
+      ++tile;
+    }
+    if (!ok) break;
+    const int next = item + gridDim.x;
+    if (next < p.num_items && item_of(p, next).qt != it.qt) ptx::mma_commit(s.aempty);
+  }
+  // Unwind: wait until every MMA issued by this thread has completed before TMEM is released.
+  ptx::mma_commit(s.drain);
+  drain_wait(s.drain, 0, p.err);
+}
+
+// ------------------------------------------------------------------------------------------
+// Epilogue (warps 0-3, one query per thread)
+// ------------------------------------------------------------------------------------------
+template <int KL>
+__device__ __forceinline__ void list_insert(uint64_t (&L)[KL], uint64_t c) {
+#pragma unroll
+  for (int i = 0; i < KL; ++i) {
+    const uint64_t lo = c < L[i] ? c : L[i];
+    const uint64_t hi = c < L[i] ? L[i] : c;
+    L[i] = lo;
+    c = hi;
+  }
+}
+
+// Smallest s that can still produce a key <= `worst` for any column of the tile; -inf accepts
+// everything (list not full, or worst = +inf / NaN).
+//   affine:  v = s*m + aux <= w with m < 0 and aux >= aux_min  =>  s >= (w - aux_min) / m
+//   scaled:  v = s*m <= w with m < 0                           =>  s >= w / m
+//   column:  v = s*aux <= w with aux in [aux_min, aux_max] < 0  =>  s >= w / aux_min (w < 0)
+//                                                                   s >= w / aux_max (w >= 0)
+// The slack (1e-5 of the magnitudes involved) keeps the bound conservative against the rounding
+// of the exact per-column evaluation in the slow path.
+__device__ __forceinline__ float s_threshold(uint64_t worst, float m, float2 ta, int kind) {
+  const float w = keys::key_value(worst);
+  if (!(w < kInf)) return -kInf;
+  float t, mag;
+  if (kind == kRankAffine) {
+    t = (w - ta.x) / m;
+    mag = fabsf(t) + (fabsf(w) + fabsf(ta.x)) / fabsf(m);
+  } else if (kind == kRankScaled) {
+    t = w / m;
+    mag = fabsf(t);
+  } else {
+    t = (w < 0.f) ? w / ta.x : w / ta.y;
+    mag = fabsf(t);
+  }
+  if (!(t == t) || !(mag < kInf)) return -kInf;
+  return t - mag * 1e-5f - 1e-30f;
+}
+
+__device__ __forceinline__ float max32(const float (&r)[32]) {
+  float a0 = ptx::fmax3(r[0], r[1], r[2]);
+  float a1 = ptx::fmax3(r[3], r[4], r[5]);
+  float a2 = ptx::fmax3(r[6], r[7], r[8]);
+  float a3 = ptx::fmax3(r[9], r[10], r[11]);
+  float a4 = ptx::fmax3(r[12], r[13], r[14]);
+  float a5 = ptx::fmax3(r[15], r[16], r[17]);
+  float a6 = ptx::fmax3(r[18], r[19], r[20]);
+  float a7 = ptx::fmax3(r[21], r[22], r[23]);
+  float a8 = ptx::fmax3(r[24], r[25], r[26]);
+  float a9 = ptx::fmax3(r[27], r[28], r[29]);
+  float b0 = ptx::fmax3(a0, a1, a2);
+  float b1 = ptx::fmax3(a3, a4, a5);
+  float b2 = ptx::fmax3(a6, a7, a8);
+  float b3 = ptx::fmax3(a9, r[30], r[31]);
+  return fmaxf(ptx::fmax3(b0, b1, b2), b3);
+}
+
+template <int KL>
+struct EpiState {
+  uint64_t L[KL];
+  float m;
+  float thr;
+  float2 ta;
+};
+
+template <int KL>
+__device__ __forceinline__ void slow_path(const FusedParams& p, float* scratch, int64_t col0,
+                                       EpiState<KL>& st) {
+  for (int j = 0; j < 32; ++j) {
+    const float sv = scratch[j];
+    if (sv < st.thr) continue;
+    const int64_t pos = col0 + j;
+    if (pos >= p.n_rows) break;
+    float v;
+    const bool allowed = p.allow == nullptr || ((p.allow[pos >> 5] >> (pos & 31)) & 1u);
+    if (!allowed) {
+      v = kInf;
+    } else if (p.rank_kind == kRankAffine) {
+      v = fmaf(sv, st.m, p.row_aux[pos]);
+    } else if (p.rank_kind == kRankScaled) {
+      v = sv * st.m;
+    } else {
+      v = sv * p.row_aux[pos];
+    }
+    const uint64_t key = keys::make_key(v, p.row_id[pos]);
+    if (key < st.L[KL - 1]) {
+      list_insert<KL>(st.L, key);
+      st.thr = s_threshold(st.L[KL - 1], st.m, st.ta, p.rank_kind);
+    }
+  }
+}
+
+template <int KL>
+__device__ __forceinline__ void process_chunk(const FusedParams& p, const float (&r)[32],
+                                              float* scratch, int64_t col0, EpiState<KL>& st) {
+  const float g = max32(r);
+  if (!(g < st.thr)) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) scratch[j] = r[j];
+    slow_path<KL>(p, scratch, col0, st);
+  }
+}
+
+template <int KL>
+__device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_base) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* scratch = reinterpret_cast<float*>(s.base + p.scratch_off) + threadIdx.x * kScratchStride;
+  const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
+  uint32_t tile = 0;
+  EpiState<KL> st;
+  for (int item = blockIdx.x; item < p.num_items; item += gridDim.x) {
+    const Item it = item_of(p, item);
+    const int64_t q = static_cast<int64_t>(it.qt) * kTileQ + warp * 32 + lane;
+    st.m = p.q_mul[q];
+#pragma unroll
+    for (int i = 0; i < KL; ++i) st.L[i] = kEmptyKey;
+    bool ok = true;
+    for (int t = it.t0; t < it.t1; ++t) {
+      const uint32_t buf = tile & 1, use = tile >> 1;
+      // Warp-uniform decision: tcgen05.ld below is warp-collective, so either every lane
+      // proceeds or every lane unwinds.
+      const bool got = ptx::mbar_wait(&s.tfull[buf], use & 1, s.abort, p.err, kErrWaitTmemFull);
+      if (!__all_sync(0xffffffffu, got)) {
+        ok = false;
+        break;
+      }
+      ptx::tc_fence_after();
+      st.ta = p.tile_aux[t];
+      st.thr = s_threshold(st.L[KL - 1], st.m, st.ta, p.rank_kind);
+      const uint32_t taddr = lane_base + buf * kTileN;
+      const int64_t col_base = static_cast<int64_t>(t) * kTileN;
+      float ra[32], rb[32];
+      ptx::tmem_ld32(taddr, ra);
+      ptx::tmem_wait_ld();
+#pragma unroll 1
+      for (int c = 0; c < 8; c += 2) {
+        ptx::tmem_ld32(taddr + (c + 1) * 32, rb);
+        process_chunk<KL>(p, ra, scratch, col_base + c * 32, st);
+        __syncwarp();  // tcgen05.ld / wait::ld are warp-collective: reconverge after the slow path
+        ptx::tmem_wait_ld();
+        if (c + 2 < 8) {
+          ptx::tmem_ld32(taddr + (c + 2) * 32, ra);
+        } else {
+          // All 8 chunks of this accumulator are in registers: hand the buffer back.
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(&s.tempty[buf]);
+        }
+        process_chunk<KL>(p, rb, scratch, col_base + (c + 1) * 32, st);
+        __syncwarp();
+        if (c + 2 < 8) ptx::tmem_wait_ld();
+      }
+      ++tile;
+    }
+    if (!ok) return;
+    uint64_t* dst = p.out + (static_cast<size_t>(q) * p.num_sc + it.sc) * KL;
+#pragma unroll
+    for (int i = 0; i < KL; ++i) dst[i] = st.L[i];
+  }
+}
+
+template <int KL>
+__global__ void __launch_bounds__(kFusedThreads, 1)
+    knn_fused_kernel(const __grid_constant__ FusedMaps maps, const __grid_constant__ FusedParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const Smem s = carve(p, smem_raw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < p.nstages; ++i) {
+      ptx::mbar_init(&s.full[i], 1);
+      ptx::mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      ptx::mbar_init(&s.tfull[i], 1);
+      ptx::mbar_init(&s.tempty[i], 4);
+    }
+    ptx::mbar_init(s.afull, 1);
+    ptx::mbar_init(s.aempty, 1);
+    ptx::mbar_init(s.drain, 1);
+    *s.abort = 0;
+    ptx::fence_barrier_init();
+  }
+  if (warp == 4 && lane == 0) {
+    ptx::tma_prefetch_desc(&maps.a64);
+    ptx::tma_prefetch_desc(&maps.b64);
+  }
+  if (warp == 5) ptx::tmem_alloc(s.tmem_slot, kTmemCols);
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *s.tmem_slot;
+  const bool lo = p.query_split != 0 && *p.q_lo_flag != 0;
+
+  if (warp == 4) {
+    if (lane == 0) run_producer(p, maps, s, lo);
+  } else if (warp == 5) {
+    if (lane == 0) run_mma(p, s, tmem_base, lo);
+    __syncwarp();
+  } else {
+    run_epilogue<KL>(p, s, tmem_base);
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+template <int KL>
+cudaError_t launch_kl(const FusedMaps& maps, const FusedParams& p, int grid, cudaStream_t stream) {
+  auto kern = knn_fused_kernel<KL>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem_bytes);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, kFusedThreads, p.smem_bytes, stream>>>(maps, p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool plan_fused_smem(FusedParams& p, int max_smem_optin) {
+  int off = 0;
+  for (int part = 0; part < 2; ++part) {
+    p.a_tx_bytes[part] = 0;
+    for (int c = 0; c < p.nchunk; ++c) {
+      const int bytes = kTileQ * p.chunk_w[c] * 2;
+      p.a_off[part][c] = off;
+      off += (bytes + 1023) & ~1023;
+      p.a_tx_bytes[part] += bytes;
+    }
+  }
+  p.stage_off = off;
+  const int scratch_bytes = kTileQ * kScratchStride * 4;
+  const int budget = max_smem_optin - 1024;  // alignment slack
+  int stages = 8;
+  for (; stages >= 2; --stages) {
+    const int bar_bytes = (2 * stages + 7) * 8 + 16;
+    const int total = off + stages * kUnitBytes + scratch_bytes + bar_bytes;
+    if (total <= budget) break;
+  }
+  if (stages < 2) return false;
+  p.nstages = stages;
+  p.scratch_off = off + stages * kUnitBytes;
+  p.bar_off = p.scratch_off + scratch_bytes;
+  p.smem_bytes = p.bar_off + (2 * stages + 7) * 8 + 16 + 1024;
+  return true;
+}
+
+cudaError_t launch_knn_fused(const FusedMaps& maps, const FusedParams& p, int kl, int grid,
+                             cudaStream_t stream) {
+  switch (kl) {
+    case 4:
+      return launch_kl<4>(maps, p, grid, stream);
+    case 8:
+      return launch_kl<8>(maps, p, grid, stream);
+    case 16:
+      return launch_kl<16>(maps, p, grid, stream);
+    case 32:
+      return launch_kl<32>(maps, p, grid, stream);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace prim
+}  // namespace ovvs

@@ -1,0 +1,105 @@
+// Fused distance + top-k kernel (sm_100a).
+//
+// Replaces the reference's dense pairwise + top-k pipeline (src/prim/mixer.cpp:843-864 with
+// prim_pairwise 174-221 and cpu_topk src/prim/cpu/cpu_prims.cpp:61-106): the nq x n score matrix
+// never exists. One CTA per SM loops over work items (query tile of 128, super-chunk of database
+// tiles of 256 rows):
+//
+//   warp 4  TMA producer   loads the query tile once per item (resident A) and streams database
+//                          K-chunks (<= 64 fp16 columns x 256 rows) through an smem ring;
+//   warp 5  MMA issuer     tcgen05.mma kind::f16, M=128 (queries) x N=256 (rows), fp32
+//                          accumulators in TMEM, double-buffered (2 x 256 columns);
+//   warps 0-3 epilogue     each thread owns one query (one TMEM lane): tcgen05.ld 32 columns at
+//                          a time, a 3-input max tree against the query's current threshold,
+//                          and, rarely, an exact per-column check + insertion into a sorted
+//                          register list of the KL best (value, row id) keys.
+//
+// Ranking values ("v", smaller is better) per query q and database position j, from the MMA dot
+// product s (queries and rows pre-scaled by powers of two, split into fp16 hi/lo parts when the
+// data is not fp16-exact):
+//   kRankAffine        v = s * m_q + aux_j     (L2 family: m_q = -2 * 2^-(e_q+e_db), aux = |y|^2)
+//   kRankScaled        v = s * m_q             (inner product / Hamming: m_q = -2^-(e_q+e_db))
+//   kRankColumnScaled  v = s * aux_j           (cosine: aux = -1/max(|y|, 1e-6))
+// Database rows are stored sorted by aux, so the per-tile range [aux_min, aux_max] turns the
+// exact test into a column-independent bound on s. Final distances are recomputed exactly from
+// the original values by the merge kernel; v only selects candidates.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+
+#include "keys.cuh"
+#include "ptx.cuh"
+
+namespace ovvs {
+namespace prim {
+
+constexpr int kTileQ = 128;                // queries per tile: MMA M, TMEM lanes
+constexpr int kTileN = 256;                // database rows per tile: MMA N
+constexpr int kUnitBytes = kTileN * 128;   // one smem slot: a 64-column fp16 chunk of a tile
+constexpr int kFusedThreads = 192;         // warps 0-3 epilogue, 4 TMA, 5 MMA
+constexpr int kMaxChunks = 8;              // padded dim <= 512 per part
+constexpr int kScratchStride = 33;         // floats per epilogue thread in the slow-path scratch
+constexpr int kTmemCols = 512;             // two 256-column fp32 accumulators
+
+enum RankKind : int { kRankAffine = 0, kRankScaled = 1, kRankColumnScaled = 2 };
+
+// Watchdog codes written to the kernel error word.
+enum WatchdogCode : int {
+  kErrNone = 0,
+  kErrWaitA = 0x101,
+  kErrWaitSlotEmpty = 0x102,
+  kErrWaitSlotFull = 0x103,
+  kErrWaitTmemEmpty = 0x104,
+  kErrWaitTmemFull = 0x105,
+  kErrWaitAEmpty = 0x106,
+  kErrDrain = 0x107,
+};
+
+struct FusedParams {
+  int dp;                          // padded dim per part (multiple of 16)
+  int nchunk;                      // K chunks per part
+  int chunk_x[kMaxChunks];         // first column of each chunk within a part
+  int chunk_w[kMaxChunks];         // chunk width in fp16 elements: 64, 32 or 16
+  int a_off[2][kMaxChunks];        // smem byte offset of query chunk (part, chunk)
+  int a_tx_bytes[2];               // bytes of one query part (all chunks)
+  int b_parts;                     // 1: rows fp16-exact; 2: rows split hi + lo
+  int nunits;                      // smem units per database tile = b_parts * nchunk
+  int nstages;                     // smem ring slots
+  int stage_off;                   // smem byte offset of slot 0
+  int scratch_off;                 // smem byte offset of the slow-path scratch
+  int bar_off;                     // smem byte offset of the mbarriers
+  int smem_bytes;                  // dynamic smem requested (includes 1 KB alignment slack)
+  int query_split;                 // 1: the query lo part is used when *q_lo_flag != 0
+  const int* q_lo_flag;            // set by the query-prep kernel
+  int num_qtiles;
+  int num_dbtiles;
+  int tiles_per_item;
+  int num_sc;                      // super-chunks (items per query tile)
+  int num_items;
+  int64_t n_rows;                  // valid database rows (positions >= n_rows are padding)
+  const float* row_aux;            // [n_pad] aux by position
+  const float2* tile_aux;          // [num_dbtiles] (min, max) of aux over the tile's valid rows
+  const uint32_t* row_id;          // [n_pad] position -> row id
+  const float* q_mul;              // [q_pad] m_q
+  const uint32_t* allow;           // [n_pad / 32] allow bits by position, or null
+  int rank_kind;
+  uint64_t* out;                   // [q_pad][num_sc][KL] sorted keys
+  int* err;                        // watchdog word
+};
+
+struct FusedMaps {
+  CUtensorMap a64, a32, a16;  // queries [q_pad, 2 * dp] fp16, boxes {64|32|16, 128}
+  CUtensorMap b64, b32, b16;  // rows    [n_pad, b_parts * dp] fp16, boxes {64|32|16, 256}
+};
+
+// Host-side launcher (knn_fused.cu). `kl` in {4, 8, 16, 32}.
+cudaError_t launch_knn_fused(const FusedMaps& maps, const FusedParams& p, int kl, int grid,
+                             cudaStream_t stream);
+
+// Fills the smem layout fields of `p` (offsets, stages) for dim `dp` split into chunks.
+// Returns false if the query tile does not fit in shared memory.
+bool plan_fused_smem(FusedParams& p, int max_smem_optin);
+
+}  // namespace prim
+}  // namespace ovvs

@@ -1,0 +1,53 @@
+// Candidate merge, exact re-ranking and cross-shard merge.
+//
+// The fused kernel leaves, per query, num_sc sorted lists of KL (ranking value, row id) keys. The
+// merge kernel keeps the KL best of their union, recomputes each survivor's distance from the
+// original values with the reference's own fp32 operation order (src/prim/mixer.cpp:174-221,
+// src/internal.hpp:215-272: sequential accumulation, no FMA contraction), and orders them by the
+// reference's top-k total order (src/prim/cpu/cpu_prims.cpp:24-32). Reported distances are
+// therefore the reference's bits whenever the same neighbours are selected.
+#pragma once
+
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace ovvs {
+namespace prim {
+
+struct MergeParams {
+  const uint64_t* cand;      // [q_pad][num_sc][kl]
+  int num_sc;
+  int kl;
+  int64_t nq;
+  int dim;
+  const float* queries;      // [nq][dim] original fp32 queries
+  const float* xn;           // [q_pad] sequential squared norms
+  int metric;                // MetricCode
+  const float* exact32;      // [n_pad][dim] by position (fp32 datasets), or null
+  const __half* rows16;      // [n_pad][rows16_stride] by position (fp16-exact datasets)
+  int rows16_stride;
+  const float* norm_sorted;  // [n_pad] sequential squared norms by position
+  const uint32_t* inv_perm;  // row id -> position
+  const uint32_t* allow;     // position-ordered allow bits, or null
+  int64_t row_offset;        // global id of local row 0
+  int k_eff;                 // output row stride and count
+  // World size 1: final results.
+  int64_t* neighbors;        // [nq][k_eff] or null
+  float* distances;          // [nq][k_eff]
+  // World size > 1: this shard's ranking values and global ids for the all-gather.
+  float* shard_rank;         // [nq][k_eff] or null
+  int64_t* shard_gid;
+  int negate_output;         // inner product: report -rank (= +dot)
+};
+
+cudaError_t launch_merge_rerank(const MergeParams& p, cudaStream_t stream);
+
+// Cross-shard merge after the all-gather: rank/gid are [world][nq][k_eff]; each shard's list is
+// sorted. Writes neighbors/distances [nq][k_eff] ordered by (rank, global id), NaN last.
+cudaError_t launch_shard_merge(const float* rank, const int64_t* gid, int world, int64_t nq,
+                               int k_eff, int negate_output, int64_t* neighbors, float* distances,
+                               cudaStream_t stream);
+
+}  // namespace prim
+}  // namespace ovvs

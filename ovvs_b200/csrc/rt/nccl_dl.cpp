@@ -1,0 +1,37 @@
+// Run-time NCCL binding (see nccl_dl.hpp).
+#include "nccl_dl.hpp"
+
+#include <dlfcn.h>
+
+#include <mutex>
+
+namespace ovvs {
+namespace rt {
+
+const NcclApi* nccl() {
+  static NcclApi api{};
+  static const NcclApi* ready = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    auto sym = [h](const char* name) { return dlsym(h, name); };
+    api.GetUniqueId = reinterpret_cast<decltype(api.GetUniqueId)>(sym("ncclGetUniqueId"));
+    api.CommInitRank = reinterpret_cast<decltype(api.CommInitRank)>(sym("ncclCommInitRank"));
+    api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(sym("ncclCommDestroy"));
+    api.CommGetAsyncError =
+        reinterpret_cast<decltype(api.CommGetAsyncError)>(sym("ncclCommGetAsyncError"));
+    api.AllGather = reinterpret_cast<decltype(api.AllGather)>(sym("ncclAllGather"));
+    api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(sym("ncclAllReduce"));
+    api.GroupStart = reinterpret_cast<decltype(api.GroupStart)>(sym("ncclGroupStart"));
+    api.GroupEnd = reinterpret_cast<decltype(api.GroupEnd)>(sym("ncclGroupEnd"));
+    if (api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.AllGather &&
+        api.AllReduce && api.GroupStart && api.GroupEnd)
+      ready = &api;
+  });
+  return ready;
+}
+
+}  // namespace rt
+}  // namespace ovvs

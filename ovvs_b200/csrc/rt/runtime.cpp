@@ -1,0 +1,195 @@
+// CUDA runtime layer (see runtime.hpp).
+#include "runtime.hpp"
+
+#include <chrono>
+#include <cstdlib>
+#include <cstring>
+#include <thread>
+
+namespace ovvs {
+namespace rt {
+
+ovvsStatus status_of(cudaError_t e) {
+  switch (e) {
+    case cudaSuccess:
+      return OVVS_STATUS_SUCCESS;
+    case cudaErrorMemoryAllocation:
+      return OVVS_STATUS_OOM;
+    case cudaErrorNoDevice:
+    case cudaErrorInsufficientDriver:
+    case cudaErrorInvalidDevice:
+    case cudaErrorNoKernelImageForDevice:
+    case cudaErrorDevicesUnavailable:
+      return OVVS_STATUS_DEVICE_UNAVAILABLE;
+    default:
+      return OVVS_STATUS_ERROR;
+  }
+}
+
+ovvsStatus status_of(ncclResult_t e) {
+  if (e == ncclSuccess) return OVVS_STATUS_SUCCESS;
+  if (e == ncclInvalidArgument || e == ncclInvalidUsage) return OVVS_STATUS_INVALID_ARGUMENT;
+  return OVVS_STATUS_ERROR;
+}
+
+DeviceBuffer::~DeviceBuffer() { release(); }
+
+cudaError_t DeviceBuffer::reserve(size_t bytes) {
+  if (bytes <= bytes_ && ptr_) return cudaSuccess;
+  release();
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  void* p = nullptr;
+  e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return e;
+  }
+  ptr_ = p;
+  bytes_ = bytes;
+  device_ = dev;
+  return cudaSuccess;
+}
+
+void DeviceBuffer::release() {
+  if (!ptr_) return;
+  int cur = -1;
+  cudaGetDevice(&cur);
+  if (device_ >= 0 && device_ != cur) cudaSetDevice(device_);
+  cudaFree(ptr_);
+  if (device_ >= 0 && device_ != cur && cur >= 0) cudaSetDevice(cur);
+  ptr_ = nullptr;
+  bytes_ = 0;
+}
+
+int default_device() {
+  const char* s = std::getenv("OVVS_CUDA_DEVICE");
+  if (s && *s) return std::atoi(s);
+  return 0;
+}
+
+void probe_device(Resources& r, int device) {
+  r.device = device;
+  r.gpu_available = false;
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count) {
+    (void)cudaGetLastError();
+    return;
+  }
+  cudaDeviceProp prop{};
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return;
+  }
+  r.device_name = prop.name;
+  r.num_sms = prop.multiProcessorCount;
+  r.max_smem_optin = static_cast<int>(prop.sharedMemPerBlockOptin);
+  // The kernels are built for sm_100a only (tcgen05 / TMEM / TMA).
+  r.gpu_available = prop.major == 10 && prop.minor == 0;
+}
+
+Resources::~Resources() {
+  if (gpu_available) cudaSetDevice(device);
+  for (auto& b : ws) b.release();
+  if (comm) ovvs::rt::nccl()->CommDestroy(comm);
+  if (d_err) cudaFree(d_err);
+  for (auto& e : phase_ev)
+    if (e) cudaEventDestroy(e);
+  if (stream) cudaStreamDestroy(stream);
+}
+
+void Resources::mark(int i) {
+  if (!profiling) return;
+  if (!phase_ev[i] && cudaEventCreate(&phase_ev[i]) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return;
+  }
+  cudaEventRecord(phase_ev[i], stream);
+  phase_valid = true;
+}
+
+ovvsStatus Resources::check_policy() const {
+  if (policy == OVVS_POLICY_FORCE_CPU || policy == OVVS_POLICY_FORCE_NPU) {
+    return OVVS_STATUS_DEVICE_UNAVAILABLE;
+  }
+  return OVVS_STATUS_SUCCESS;
+}
+
+ovvsStatus Resources::activate() {
+  if (!gpu_available) return OVVS_STATUS_DEVICE_UNAVAILABLE;
+  OVVS_TRY_CUDA(cudaSetDevice(device));
+  if (!stream) OVVS_TRY_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+  if (!d_err) {
+    OVVS_TRY_CUDA(cudaMalloc(&d_err, sizeof(int)));
+    OVVS_TRY_CUDA(cudaMemset(d_err, 0, sizeof(int)));
+  }
+  return OVVS_STATUS_SUCCESS;
+}
+
+ovvsStatus Resources::finish() {
+  OVVS_TRY_CUDA(cudaStreamSynchronize(stream));
+  int err = 0;
+  OVVS_TRY_CUDA(cudaMemcpy(&err, d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err != 0) {
+    cudaMemset(d_err, 0, sizeof(int));
+    return OVVS_STATUS_ERROR;
+  }
+  return OVVS_STATUS_SUCCESS;
+}
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      (void)cudaGetLastError();
+      return static_cast<EncodeTiledFn>(nullptr);
+    }
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+}  // namespace
+
+bool encode_f16_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows,
+                   uint32_t box_cols, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  const uint32_t row_bytes = box_cols * 2;
+  const CUtensorMapSwizzle sw = row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : row_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                  : CU_TENSOR_MAP_SWIZZLE_32B;
+  std::memset(map, 0, sizeof(*map));
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            elem, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+ovvsStatus allreduce_i64_sum(Resources& r, int64_t* value) {
+  if (r.world <= 1) return OVVS_STATUS_SUCCESS;
+  int64_t* d = nullptr;
+  OVVS_TRY(r.scratch<int64_t>(kWsFlags, 1, &d));
+  OVVS_TRY_CUDA(cudaMemcpyAsync(d, value, sizeof(int64_t), cudaMemcpyHostToDevice, r.stream));
+  OVVS_TRY(status_of(ovvs::rt::nccl()->AllReduce(d, d, 1, ncclInt64, ncclSum, r.comm, r.stream)));
+  OVVS_TRY_CUDA(cudaMemcpyAsync(value, d, sizeof(int64_t), cudaMemcpyDeviceToHost, r.stream));
+  OVVS_TRY_CUDA(cudaStreamSynchronize(r.stream));
+  return OVVS_STATUS_SUCCESS;
+}
+
+}  // namespace rt
+}  // namespace ovvs

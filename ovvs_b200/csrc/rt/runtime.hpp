@@ -1,0 +1,143 @@
+// CUDA runtime layer behind the ovvs C ABI: the Resources object (device, stream, NCCL
+// communicator, workspace, watchdog word), device/pinned buffers, tensor-map encoding and the
+// mapping from CUDA/NCCL errors to ovvsStatus.
+//
+// Replaces the reference's ResourcesData (src/internal.hpp:459-562) and its device probing
+// (src/rt/probe.cpp:132-140): one Resources = one CUDA device + one stream; there is no device
+// selection between backends and no CPU fallback.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <atomic>
+#include <cstdint>
+#include <mutex>
+#include <string>
+
+#include "nccl_dl.hpp"
+#include "ovvs/ovvs.h"
+
+struct ovvsResourcesImpl;
+
+namespace ovvs {
+namespace rt {
+
+ovvsStatus status_of(cudaError_t e);
+ovvsStatus status_of(ncclResult_t e);
+
+#define OVVS_TRY_CUDA(expr)                                   \
+  do {                                                        \
+    const cudaError_t ovvs_e_ = (expr);                       \
+    if (ovvs_e_ != cudaSuccess) return ::ovvs::rt::status_of(ovvs_e_); \
+  } while (0)
+
+#define OVVS_TRY(expr)                                        \
+  do {                                                        \
+    const ovvsStatus ovvs_s_ = (expr);                        \
+    if (ovvs_s_ != OVVS_STATUS_SUCCESS) return ovvs_s_;       \
+  } while (0)
+
+// Grow-only device allocation on one device.
+class DeviceBuffer {
+ public:
+  DeviceBuffer() = default;
+  ~DeviceBuffer();
+  DeviceBuffer(const DeviceBuffer&) = delete;
+  DeviceBuffer& operator=(const DeviceBuffer&) = delete;
+  // Ensures at least `bytes` are allocated (contents are not preserved on growth).
+  cudaError_t reserve(size_t bytes);
+  void release();
+  void* get() const { return ptr_; }
+  size_t size() const { return bytes_; }
+  template <class T>
+  T* as() const {
+    return static_cast<T*>(ptr_);
+  }
+
+ private:
+  void* ptr_ = nullptr;
+  size_t bytes_ = 0;
+  int device_ = -1;
+};
+
+// Workspace slots owned by a Resources (reused across calls on that Resources).
+enum WorkSlot : int {
+  kWsQueries = 0,  // fp32 queries
+  kWsQueryA,       // fp16 hi/lo query operand
+  kWsQueryMul,
+  kWsQueryNorm,
+  kWsFlags,        // lo flag
+  kWsBitset,       // caller bitset (host searches)
+  kWsAllow,        // position-ordered allow bits
+  kWsCand,         // fused-kernel candidate lists
+  kWsNeighbors,    // results (host searches)
+  kWsDistances,
+  kWsShardRank,    // per-shard results for the all-gather
+  kWsShardGid,
+  kWsGatherRank,
+  kWsGatherGid,
+  kWsCount
+};
+
+struct Resources {
+  int device = 0;
+  bool gpu_available = false;
+  int num_sms = 0;
+  int max_smem_optin = 0;
+  std::string device_name = "no-cuda-device";
+  ovvsPolicy policy = OVVS_POLICY_AUTO;
+  std::atomic<ovvsDevice> last_device{OVVS_DEVICE_CPU};
+  ovvsDType last_compute_dtype = OVVS_DTYPE_F32;
+  bool cagra_walk_counters = false;
+  cudaStream_t stream = nullptr;
+  int rank = 0;
+  int world = 1;
+  ncclComm_t comm = nullptr;
+  int* d_err = nullptr;  // kernel watchdog word (device)
+  static constexpr int kPhases = 4;
+  bool profiling = false;
+  bool phase_valid = false;
+  cudaEvent_t phase_ev[kPhases + 1] = {};
+  std::mutex mu;
+  DeviceBuffer ws[kWsCount];
+
+  ~Resources();
+  // Makes `device` current on the calling thread and creates the stream / error word on first
+  // use. Returns DEVICE_UNAVAILABLE without a usable sm_100 device.
+  ovvsStatus activate();
+  // FORCE_CPU / FORCE_NPU cannot be honoured: the forced device never falls back.
+  ovvsStatus check_policy() const;
+  // Waits for the stream, then reads and clears the watchdog word.
+  ovvsStatus finish();
+  // Records phase boundary `i` (0..kPhases) of the current search when profiling.
+  void mark(int i);
+  template <class T>
+  ovvsStatus scratch(WorkSlot slot, size_t count, T** out) {
+    const cudaError_t e = ws[slot].reserve(count * sizeof(T) + 16);
+    if (e != cudaSuccess) return status_of(e);
+    *out = ws[slot].as<T>();
+    return OVVS_STATUS_SUCCESS;
+  }
+};
+
+inline Resources* from_handle(ovvsResources_t r) { return reinterpret_cast<Resources*>(r); }
+inline ovvsResources_t to_handle(Resources* r) { return reinterpret_cast<ovvsResources_t>(r); }
+
+// Probes `device` and fills the device fields of `r` (no stream yet).
+void probe_device(Resources& r, int device);
+
+// 2D fp16 tensor map over a row-major [rows x cols] matrix with a {box_cols x box_rows} box and
+// the swizzle that matches box_cols * 2 bytes (128/64/32).
+bool encode_f16_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows,
+                   uint32_t box_cols, uint32_t box_rows);
+
+// Global row count of a sharded dataset (sum over ranks) and other small all-reduces.
+ovvsStatus allreduce_i64_sum(Resources& r, int64_t* value);
+
+// Default CUDA device for ovvsResourcesCreate: OVVS_CUDA_DEVICE, else 0.
+int default_device();
+
+}  // namespace rt
+}  // namespace ovvs

@@ -1,0 +1,178 @@
+"""Generates the golden fixtures in tests/golden/*.npz by running the REFERENCE library.
+
+The reference (manan-ramnani/ovVS 0.2.0) is compiled from its own sources by oracle/Makefile into
+oracle/_ref/libovvs_ref.so and driven through its public C ABI with policy FORCE_CPU. Each fixture
+stores the inputs and the reference's outputs, so the tests need neither the reference checkout
+nor its build on the GPU box.
+
+Run from the repository root:  python tests/golden/make_golden.py
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, ROOT)
+
+from oracle.cpu import Reference, make_data  # noqa: E402
+
+OUT = os.path.dirname(os.path.abspath(__file__))
+METRIC_IDS = {"l2": 0, "l2_sqrt": 1, "inner_product": 2, "cosine": 3, "hamming": 4, "lp": 5,
+              "unknown7": 7}
+
+
+def trunc_f16(x: np.ndarray) -> np.ndarray:
+    """Truncating fp32->fp16 of the reference tests (internal.hpp:831-840 and
+    tests/test_neighbors.cpp:3636-3646), vectorised."""
+    b = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.int64)
+    sign = (b >> 16) & 0x8000
+    exp = ((b >> 23) & 0xFF) - 127 + 15
+    man = b & 0x7FFFFF
+    out = np.where(exp <= 0, sign,
+                   np.where(exp >= 31, sign | 0x7C00, sign | (np.clip(exp, 0, 31) << 10) | (man >> 13)))
+    return out.astype(np.uint16)
+
+
+def brute_cases(rng):
+    """(name, data, dtype, queries, k, metric, bitset, out_fill)."""
+    cases = []
+    # --- the reference's own hot-path test scenarios (tests/test_neighbors.cpp) ---
+    cases.append(("recall_one_l2", make_data(40, 8, 100), "f32", make_data(5, 8, 101), 4, "l2",
+                  None, None))
+    tri = np.array([[1, 0], [0, 1], [-1, 0]], np.float32)
+    q10 = np.array([[1, 0]], np.float32)
+    cases.append(("known_ip", tri, "f32", q10, 2, "inner_product", None, None))
+    cases.append(("known_cosine", tri, "f32", q10, 2, "cosine", None, None))
+    d16 = make_data(16, 4, 112)
+    q16 = make_data(1, 4, 113)
+    allow = np.zeros(2, np.uint8)
+    for a in (2, 5, 9, 12):
+        allow[a >> 3] |= 1 << (a & 7)
+    cases.append(("allow_list_l2", d16, "f32", q16, 3, "l2", allow, None))
+    cases.append(("allow_list_hamming", d16, "f32", q16, 3, "hamming", None, None))
+    cases.append(("allow_list_lp", d16, "f32", q16, 3, "lp", None, None))
+    d20 = make_data(20, 4, 110)
+    even = np.zeros(3, np.uint8)
+    for i in range(0, 20, 2):
+        even[i >> 3] |= 1 << (i & 7)
+    cases.append(("bitset_even", d20, "f32", make_data(1, 4, 111), 3, "l2", even, None))
+    d480 = make_data(20, 8, 480)
+    cases.append(("typed_f16_trunc", trunc_f16(d480), "f16", make_data(1, 8, 481), 4, "l2", None,
+                  None))
+    i8 = np.clip(np.round(d480 * 50.0), -127, 127).astype(np.int8)
+    cases.append(("typed_i8", i8, "i8", make_data(1, 8, 481), 4, "l2", None, None))
+    cons = (((np.arange(48) * 17) % 100) / np.float32(50.0) - np.float32(1.0)).astype(np.float32)
+    cases.append(("consumer_c", cons.reshape(12, 4), "f32",
+                  np.array([[0.1, -0.2, 0.3, 0.0]], np.float32), 3, "l2", None, None))
+
+    # --- randomized coverage of every metric path ---
+    X = rng.standard_normal((257, 40)).astype(np.float32)
+    Q = rng.standard_normal((11, 40)).astype(np.float32)
+    for m in METRIC_IDS:
+        for k in (1, 10):
+            cases.append((f"rand_{m}_k{k}", X, "f32", Q, k, m, None, None))
+    U = rng.random((300, 64), dtype=np.float32)
+    QU = rng.random((7, 64), dtype=np.float32)
+    cases.append(("uniform_l2_k16", U, "f32", QU, 16, "l2", None, None))
+    # typed datasets
+    G = rng.standard_normal((300, 64)).astype(np.float32) * 3
+    cases.append(("f16_rne_l2", G.astype(np.float16).view(np.uint16), "f16",
+                  rng.standard_normal((9, 64)).astype(np.float32), 10, "l2", None, None))
+    cases.append(("f16_rne_ip", G.astype(np.float16).view(np.uint16), "f16",
+                  rng.standard_normal((9, 64)).astype(np.float32), 10, "inner_product", None,
+                  None))
+    B = rng.integers(0, 256, (200, 24), dtype=np.uint8)
+    QB = rng.integers(0, 256, (5, 24)).astype(np.float32)
+    cases.append(("u8_l2", B, "u8", QB, 8, "l2", None, None))
+    cases.append(("f8e4m3_as_u8_l2", B, "f8e4m3", QB, 8, "l2", None, None))
+    cases.append(("i8_cosine", B.view(np.int8), "i8", QB - 128, 8, "cosine", None, None))
+    # k > n: output stride min(k, n), IP negates nq*k entries of caller memory
+    S = rng.standard_normal((6, 5)).astype(np.float32)
+    QS = rng.standard_normal((3, 5)).astype(np.float32)
+    for m in ("l2", "inner_product"):
+        cases.append((f"k_gt_n_{m}", S, "f32", QS, 9, m, None, (5, 7.0)))
+    # fewer allowed rows than k: filtered rows come back as +inf (-inf for IP), by row id
+    F = rng.standard_normal((40, 8)).astype(np.float32)
+    QF = rng.standard_normal((4, 8)).astype(np.float32)
+    few = np.zeros(5, np.uint8)
+    for a in (3, 17, 30):
+        few[a >> 3] |= 1 << (a & 7)
+    for m in ("l2", "inner_product", "cosine"):
+        cases.append((f"few_allowed_{m}", F, "f32", QF, 6, m, few, None))
+    # exact duplicates (ties by lower id), zero rows, NaN and inf rows (NaN last)
+    Dd = rng.standard_normal((64, 12)).astype(np.float32)
+    Dd[10] = Dd[3]
+    Dd[40] = Dd[3]
+    Dd[20] = 0.0
+    Dd[21] = 0.0
+    Dd[50, 4] = np.nan
+    Dd[51, 0] = np.inf
+    Qd = np.vstack([Dd[3:4], rng.standard_normal((4, 12)).astype(np.float32)])
+    for m in ("l2", "inner_product", "cosine", "l2_sqrt"):
+        cases.append((f"ties_nan_{m}", Dd, "f32", Qd, 64, m, None, None))
+    return cases
+
+
+def kmeans_cases(rng):
+    cases = []
+    blobs = make_data(60, 4, 600)
+    blobs[:30, 0] += 5.0  # tests/test_cluster.cpp:15-17
+    cases.append(("two_blobs", blobs, 2, 15))
+    centres = rng.normal(0, 3, (64, 32)).astype(np.float32)
+    lab = rng.integers(0, 64, 3000)
+    mix = (centres[lab] + rng.standard_normal((3000, 32)).astype(np.float32)).astype(np.float32)
+    cases.append(("mixture_3000x32_k64", mix, 64, 10))
+    cases.append(("k_gt_n", rng.standard_normal((20, 6)).astype(np.float32), 30, 3))
+    cases.append(("iters0", mix[:500], 16, 0))
+    return cases
+
+
+def main():
+    ref = Reference()
+    rng = np.random.default_rng(20261201)
+    brute = {}
+    for (name, data, dtype, q, k, metric, bitset, fill) in brute_cases(rng):
+        nb, ds = ref.brute_search(data, q, k, metric=METRIC_IDS[metric] if metric in METRIC_IDS
+                                  else metric, dtype=dtype, bitset=bitset, out_fill=fill)
+        p = f"{name}__"
+        brute[p + "data"] = np.ascontiguousarray(data)
+        brute[p + "dtype"] = np.array(dtype)
+        brute[p + "queries"] = np.ascontiguousarray(q, np.float32)
+        brute[p + "k"] = np.array(k)
+        brute[p + "metric"] = np.array(METRIC_IDS[metric])
+        brute[p + "bitset"] = np.zeros(0, np.uint8) if bitset is None else bitset
+        brute[p + "fill"] = np.array([-1, 0.0] if fill is None else list(fill), np.float64)
+        brute[p + "neighbors"] = nb
+        brute[p + "distances"] = ds
+    np.savez_compressed(os.path.join(OUT, "brute_force.npz"), **brute)
+
+    km = {}
+    for (name, x, k, iters) in kmeans_cases(rng):
+        cents, kk, labels, dist = ref.kmeans(x, k, iters, predict=k <= x.shape[0])
+        p = f"{name}__"
+        km[p + "x"] = x
+        km[p + "nclusters"] = np.array(k)
+        km[p + "iters"] = np.array(iters)
+        km[p + "centroids"] = cents
+        km[p + "reported_k"] = np.array(kk)
+        km[p + "labels"] = labels
+        km[p + "distances"] = dist
+    np.savez_compressed(os.path.join(OUT, "kmeans.npz"), **km)
+
+    # top-k total order (cpu_prims.cpp:24-32) on the reference's own edge values
+    scores = np.array([[np.nan, 0.0, -0.0, np.inf, -np.inf, 1.0, 1.0, np.nan]], np.float32)
+    idx, val = ref.topk(scores, 8, largest=False)
+    bs = ref.bitset_from_allow_list(20, np.array([2, 5, 9, 12, -1, 25, 19], np.int64))
+    np.savez_compressed(os.path.join(OUT, "misc.npz"), topk_scores=scores, topk_idx=idx,
+                        topk_val=val, bitset_ids=np.array([2, 5, 9, 12, -1, 25, 19], np.int64),
+                        bitset_n=np.array(20), bitset=bs,
+                        version=np.array(ref.lib.ovvsGetVersion().decode()))
+    print("wrote", sorted(f for f in os.listdir(OUT) if f.endswith(".npz")))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,76 @@
+"""The CPU oracle (oracle/ovvs_oracle.cpp) against the reference's own outputs.
+
+tests/golden/*.npz were produced by the reference library compiled from its sources
+(tests/golden/make_golden.py), so a bit-exact match here pins the restatement to the reference.
+"""
+
+import os
+
+import numpy as np
+import pytest
+
+from tests.helpers import assert_search_equal, same_bits
+
+
+def _brute_case(c, oracle):
+    data32 = oracle.convert_to_f32(str(c["dtype"]), c["data"])
+    bitset = c["bitset"] if c["bitset"].size else None
+    fill = None
+    if float(c["fill"][0]) != -1 or float(c["fill"][1]) != 0.0:
+        fill = (int(c["fill"][0]), float(c["fill"][1]))
+    return oracle.brute_search(data32, c["queries"], int(c["k"]), int(c["metric"]), bitset=bitset,
+                               out_fill=fill)
+
+
+def test_brute_force_cases_bit_exact(golden_brute, oracle):
+    assert len(golden_brute) >= 39
+    for name, c in golden_brute.items():
+        nb, ds = _brute_case(c, oracle)
+        assert_search_equal(nb, ds, c["neighbors"], c["distances"], what=name)
+
+
+def test_kmeans_cases_bit_exact(golden_kmeans, oracle):
+    for name, c in golden_kmeans.items():
+        x = c["x"]
+        cents = oracle.kmeans_fit(x, int(c["nclusters"]), max(4, int(c["iters"])))
+        assert np.all(same_bits(cents, c["centroids"])), name
+        assert int(c["reported_k"]) == int(c["nclusters"]), name
+        if c["labels"].size:
+            labels, dist = oracle.kmeans_predict(cents, x)
+            assert np.array_equal(labels, c["labels"]), name
+            assert np.all(same_bits(dist, c["distances"])), name
+
+
+def test_topk_total_order(golden_misc, oracle):
+    idx, val = oracle.topk(golden_misc["topk_scores"], 8)
+    assert np.array_equal(idx, golden_misc["topk_idx"])
+    assert np.all(same_bits(val, golden_misc["topk_val"]))
+
+
+def test_bitset_from_allow_list(golden_misc, oracle):
+    bs = oracle.bitset_from_allow_list(int(golden_misc["bitset_n"]), golden_misc["bitset_ids"])
+    assert np.array_equal(bs, golden_misc["bitset"])
+
+
+def test_kmeans_init_rows_follow_mt19937(oracle):
+    # mixer.cpp:880-890: the first draw of std::mt19937(42) through uniform_int_distribution
+    rows = oracle.kmeans_init_rows(1000, 16)
+    assert rows.shape == (16,) and len(set(rows.tolist())) == 16
+    assert np.all((rows >= 0) & (rows < 1000))
+    assert np.array_equal(rows, oracle.kmeans_init_rows(1000, 16))
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(os.path.dirname(__file__), "..", "oracle", "_ref",
+                                                    "libovvs_ref.so")),
+                    reason="reference library not built in this checkout")
+@pytest.mark.parametrize("metric", ["l2", "inner_product", "cosine", "l2_sqrt", "hamming", "lp"])
+def test_reference_library_matches_oracle(oracle, metric):
+    from oracle.cpu import Reference
+
+    ref = Reference()
+    rng = np.random.default_rng(7)
+    X = rng.standard_normal((3000, 24)).astype(np.float32)
+    Q = rng.standard_normal((20, 24)).astype(np.float32)
+    a = oracle.brute_search(X, Q, 12, metric)
+    b = ref.brute_search(X, Q, 12, metric)
+    assert_search_equal(a[0], a[1], b[0], b[1], what=metric)
