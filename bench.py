@@ -42,6 +42,10 @@ CONFIGS = {
     "c3": dict(metric="l2", dtype="f16", n=10_000_000, dim=128, nq=10_000, k=10, dist="mixture",
                centres=1024, centre_std=2.0, seed=2,
                desc="L2 fp16, N=10M x 128 Gaussian mixture (1024 centres, var 4), Q=10k, k=10"),
+    # profiling case: config 3's distribution and queries with 2M rows (512 MB, > L2)
+    "c3s": dict(metric="l2", dtype="f16", n=2_000_000, dim=128, nq=10_000, k=10, dist="mixture",
+                centres=1024, centre_std=2.0, seed=2,
+                desc="L2 fp16, N=2M x 128 Gaussian mixture (1024 centres), Q=10k, k=10"),
     "c5": dict(metric="inner_product", dtype="f16", n=100_000_000, dim=96, nq=100_000, k=100,
                dist="unit", seed=4, desc="IP fp16, N=100M x 96 unit-norm, Q=100k, k=100"),
 }
@@ -269,6 +273,7 @@ def run_ours(args, cfg):
     import torch.distributed as dist
 
     import ovvs_b200 as ov
+    from ovvs_b200.shard import row_range
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -301,7 +306,7 @@ def run_ours(args, cfg):
         return float(t.item())
 
     n, dim, nq, k = cfg["n"], cfg["dim"], cfg["nq"], cfg["k"]
-    lo, hi = rank * n // world, (rank + 1) * n // world
+    lo, hi = row_range(rank, world, n)
     shard = _gen_rows(cfg, lo, hi, dev, torch)
     shard_host = shard.cpu().numpy()
     if cfg["dtype"] == "f16":

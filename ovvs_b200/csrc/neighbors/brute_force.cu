@@ -257,6 +257,12 @@ ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_
   uint64_t* cand = nullptr;
   OVVS_TRY(r.scratch(rt::kWsCand, static_cast<size_t>(q_pad) * p.num_sc * kl, &cand));
   p.out = cand;
+  uint64_t* bound = nullptr;
+  OVVS_TRY(r.scratch(rt::kWsBound, static_cast<size_t>(q_pad), &bound));
+  OVVS_TRY_CUDA(cudaMemsetAsync(bound, 0xFF, static_cast<size_t>(q_pad) * sizeof(uint64_t), s));
+  p.q_bound = bound;
+  p.nq = nq;
+  p.k_pub = static_cast<int>(k_eff);
 
   prim::FusedMaps maps{};
   const uint64_t a_cols = static_cast<uint64_t>(2 * ix.dp);

@@ -210,16 +210,15 @@ __device__ __forceinline__ void list_insert(uint64_t (&L)[KL], uint64_t c) {
   }
 }
 
-// Smallest s that can still produce a key <= `worst` for any column of the tile; -inf accepts
-// everything (list not full, or worst = +inf / NaN).
+// Smallest s that can still produce a ranking value <= w for any column of the tile; -inf
+// accepts everything (w = +inf or NaN: nothing to compare against yet).
 //   affine:  v = s*m + aux <= w with m < 0 and aux >= aux_min  =>  s >= (w - aux_min) / m
 //   scaled:  v = s*m <= w with m < 0                           =>  s >= w / m
 //   column:  v = s*aux <= w with aux in [aux_min, aux_max] < 0  =>  s >= w / aux_min (w < 0)
 //                                                                   s >= w / aux_max (w >= 0)
 // The slack (1e-5 of the magnitudes involved) keeps the bound conservative against the rounding
 // of the exact per-column evaluation in the slow path.
-__device__ __forceinline__ float s_threshold(uint64_t worst, float m, float2 ta, int kind) {
-  const float w = keys::key_value(worst);
+__device__ __forceinline__ float s_threshold(float w, float m, float2 ta, int kind) {
   if (!(w < kInf)) return -kInf;
   float t, mag;
   if (kind == kRankAffine) {
@@ -258,16 +257,61 @@ template <int KL>
 struct EpiState {
   uint64_t L[KL];
   float m;
-  float thr;
+  float thr;      // s-space threshold for the current tile
+  float gw;       // ranking value of the shared per-query bound (+ slack), NaN when none
   float2 ta;
+  bool real;      // this lane holds a real query
 };
 
+// Ranking value the filter compares against: the list's own worst entry, tightened by the
+// shared per-query bound. The bound gets a relative slack of 1e-5 of the magnitudes involved so
+// that rows tied with it within the ranking values' rounding still pass (the exact re-rank then
+// orders them).
 template <int KL>
-__device__ __forceinline__ void slow_path(const FusedParams& p, float* scratch, int64_t col0,
-                                       EpiState<KL>& st) {
+__device__ __forceinline__ void refresh_threshold(EpiState<KL>& st, int kind) {
+  if (!st.real) {
+    st.thr = kInf;  // padding lanes never select
+    return;
+  }
+  const float own = keys::key_value(st.L[KL - 1]);  // NaN while the list is not full
+  st.thr = s_threshold(fminf(own, st.gw), st.m, st.ta, kind);
+}
+
+template <int KL>
+__device__ __forceinline__ void read_bound(const FusedParams& p, int64_t q, EpiState<KL>& st) {
+  const uint64_t b = __ldcg(reinterpret_cast<const unsigned long long*>(p.q_bound + q));
+  const float w = keys::key_value(b);
+  const float mag = fabsf(w) + fabsf(st.ta.x) + fabsf(st.ta.y);
+  st.gw = w + mag * 1e-5f;
+}
+
+template <int KL>
+__device__ __forceinline__ void publish_bound(const FusedParams& p, int64_t q,
+                                              const EpiState<KL>& st) {
+  // Branch-free selection keeps the list in registers (a select chain would be turned into an
+  // indexed load, which moves the whole list to local memory).
+  uint64_t kth = 0;
+#pragma unroll
+  for (int i = 0; i < KL; ++i) kth |= st.L[i] & (0ull - static_cast<uint64_t>(i == p.k_pub - 1));
+  if (kth != kEmptyKey) atomicMin(reinterpret_cast<unsigned long long*>(p.q_bound + q), kth);
+}
+
+template <int KL>
+__device__ __forceinline__ void slow_path(const FusedParams& p, const float (&r)[32],
+                                          float* scratch, int64_t col0, EpiState<KL>& st) {
+  // Visit only the columns that pass the conservative bound (NaN passes: its exact key is
+  // decided below).
+  uint32_t mask = 0;
+#pragma unroll
   for (int j = 0; j < 32; ++j) {
+    mask |= static_cast<uint32_t>(!(r[j] < st.thr)) << j;
+    scratch[j] = r[j];
+  }
+  while (mask) {
+    const int j = __ffs(mask) - 1;
+    mask &= mask - 1;
     const float sv = scratch[j];
-    if (sv < st.thr) continue;
+    if (sv < st.thr) continue;  // threshold tightened by an earlier insertion
     const int64_t pos = col0 + j;
     if (pos >= p.n_rows) break;
     float v;
@@ -284,7 +328,7 @@ __device__ __forceinline__ void slow_path(const FusedParams& p, float* scratch, 
     const uint64_t key = keys::make_key(v, p.row_id[pos]);
     if (key < st.L[KL - 1]) {
       list_insert<KL>(st.L, key);
-      st.thr = s_threshold(st.L[KL - 1], st.m, st.ta, p.rank_kind);
+      refresh_threshold<KL>(st, p.rank_kind);
     }
   }
 }
@@ -293,11 +337,7 @@ template <int KL>
 __device__ __forceinline__ void process_chunk(const FusedParams& p, const float (&r)[32],
                                               float* scratch, int64_t col0, EpiState<KL>& st) {
   const float g = max32(r);
-  if (!(g < st.thr)) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) scratch[j] = r[j];
-    slow_path<KL>(p, scratch, col0, st);
-  }
+  if (!(g < st.thr)) slow_path<KL>(p, r, scratch, col0, st);
 }
 
 template <int KL>
@@ -311,6 +351,9 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
     const Item it = item_of(p, item);
     const int64_t q = static_cast<int64_t>(it.qt) * kTileQ + warp * 32 + lane;
     st.m = p.q_mul[q];
+    st.real = q < p.nq;
+    st.ta = p.tile_aux[it.t0];
+    read_bound<KL>(p, q, st);
 #pragma unroll
     for (int i = 0; i < KL; ++i) st.L[i] = kEmptyKey;
     bool ok = true;
@@ -325,7 +368,11 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
       }
       ptx::tc_fence_after();
       st.ta = p.tile_aux[t];
-      st.thr = s_threshold(st.L[KL - 1], st.m, st.ta, p.rank_kind);
+      if (((t - it.t0) & (kBoundPeriod - 1)) == kBoundPeriod - 1 && st.real) {
+        publish_bound<KL>(p, q, st);
+        read_bound<KL>(p, q, st);
+      }
+      refresh_threshold<KL>(st, p.rank_kind);
       const uint32_t taddr = lane_base + buf * kTileN;
       const int64_t col_base = static_cast<int64_t>(t) * kTileN;
       float ra[32], rb[32];
@@ -352,6 +399,7 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
       ++tile;
     }
     if (!ok) return;
+    if (st.real) publish_bound<KL>(p, q, st);
     uint64_t* dst = p.out + (static_cast<size_t>(q) * p.num_sc + it.sc) * KL;
 #pragma unroll
     for (int i = 0; i < KL; ++i) dst[i] = st.L[i];

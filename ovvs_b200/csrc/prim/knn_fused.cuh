@@ -84,9 +84,18 @@ struct FusedParams {
   const float* q_mul;              // [q_pad] m_q
   const uint32_t* allow;           // [n_pad / 32] allow bits by position, or null
   int rank_kind;
+  int64_t nq;                      // real queries (lanes >= nq are padding and never select)
+  int k_pub;                       // rank (1-based) whose key a list publishes as a bound
+  uint64_t* q_bound;               // [q_pad] smallest published k_pub-th key per query
   uint64_t* out;                   // [q_pad][num_sc][KL] sorted keys
   int* err;                        // watchdog word
 };
+
+// Every kBoundPeriod tiles each epilogue thread publishes its list's k_pub-th key to q_bound
+// (atomicMin) and re-reads the minimum. Any list's k_pub-th key is an upper bound on the
+// k_pub-th best key of the whole database for that query, so lists of other work items (which
+// start empty) filter with it from their first tile on.
+constexpr int kBoundPeriod = 16;
 
 struct FusedMaps {
   CUtensorMap a64, a32, a16;  // queries [q_pad, 2 * dp] fp16, boxes {64|32|16, 128}

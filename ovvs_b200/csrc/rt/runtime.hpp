@@ -72,6 +72,7 @@ enum WorkSlot : int {
   kWsBitset,       // caller bitset (host searches)
   kWsAllow,        // position-ordered allow bits
   kWsCand,         // fused-kernel candidate lists
+  kWsBound,        // shared per-query bound of the fused kernel
   kWsNeighbors,    // results (host searches)
   kWsDistances,
   kWsShardRank,    // per-shard results for the all-gather

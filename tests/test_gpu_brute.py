@@ -84,6 +84,13 @@ def _run_parity(ovvs, gpu, oracle, metric, dtype, n, dim, nq, k, kind="gauss", s
             v = np.float32(np.inf)
         return -v if metric == "inner_product" else v
 
+    if metric == "lp":
+        # The reference takes (sum |x-y|^p)^(1/p) with glibc powf, which is not correctly rounded
+        # for the 1/2 power (1 ulp off sqrtf in ~0.06% of inputs); this library uses the
+        # correctly rounded square root. Same ranking input, distances within 1 ulp.
+        assert np.array_equal(nb, rnb), "lp ids"
+        assert np.allclose(ds, rds, rtol=2.5e-7, atol=0), "lp distances beyond 1 ulp"
+        return
     assert_search_close(nb, ds, rnb, rds, k_eff, exact, TOL[dtype],
                         what=f"{metric}/{dtype}/{n}x{dim}/q{nq}/k{k}", atol_floor=1.0)
 
