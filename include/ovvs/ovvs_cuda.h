@@ -47,6 +47,29 @@ OVVS_API ovvsStatus ovvsBruteForceSearchDevice(ovvsResources_t res, ovvsBruteFor
                                                const uint8_t* d_bitset, int64_t* d_neighbors,
                                                float* d_distances);
 
+/* Same search as ovvsBruteForceSearchDevice for callers that cannot let a library allocate GPU
+   memory -- e.g. a process whose free device memory is already reserved by another allocator
+   (a framework's caching pool), or a latency-critical request loop where cudaMalloc/cudaFree and
+   their implicit device synchronisation are not acceptable. This entry point has no counterpart
+   in the reference. It allocates nothing: all intermediate buffers come from a fixed 32 MiB
+   device array built into the library (the runtime creates it once per device when the library's
+   module is loaded; it lives until the process exits). Its device address is looked up on the
+   first call on each device, so make that first call before any stream capture. Work runs on
+   `stream` (NULL = the default stream) and the call returns after it has finished. Sizes whose
+   buffers do not fit the array (about 4*dim + 16 + 8*list bytes per query, list = k plus a small
+   margin rounded up to 4/8/16/32: some 50k queries of dim 128 at k = 10) are rejected with
+   OVVS_STATUS_SHAPE_MISMATCH;
+   sharded indexes and k above the register-list limit return OVVS_STATUS_UNSUPPORTED. All calls on
+   a device share the array and keep the last call's contents; the library clears what must start
+   empty and serialises its own calls per device, because calls whose GPU work overlapped on the
+   same array would race. */
+OVVS_API ovvsStatus ovvsBruteForceSearchDeviceNoAlloc(ovvsResources_t res,
+                                                      ovvsBruteForceIndex_t index,
+                                                      const float* d_queries, int64_t nq,
+                                                      int64_t k, const uint8_t* d_bitset,
+                                                      int64_t* d_neighbors, float* d_distances,
+                                                      void* stream);
+
 /* ---- one process per GPU ------------------------------------------------------------------ */
 
 /* Size in bytes of the NCCL unique id that ovvsNcclUniqueId writes (128). */

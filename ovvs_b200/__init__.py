@@ -86,6 +86,8 @@ def _bind(lib):
         "ovvsResourcesDevice": ([c_void_p, P(c_int32)], c_int32),
         "ovvsBruteForceSearchDevice": ([c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
                                         c_void_p, c_void_p], c_int32),
+        "ovvsBruteForceSearchDeviceNoAlloc": ([c_void_p, c_void_p, c_void_p, c_int64, c_int64,
+                                               c_void_p, c_void_p, c_void_p, c_void_p], c_int32),
         "ovvsResourcesSetProfiling": ([c_void_p, c_int32], c_int32),
         "ovvsResourcesLastPhaseMs": ([c_void_p, P(c_float), c_int32], c_int32),
         "ovvsNcclUniqueIdSize": ([], c_int32),
@@ -316,6 +318,17 @@ class BruteIndex:
         _check(lib().ovvsBruteForceSearchDevice(self._res._h, self._h, qp, nq, k,
                                                 _dev_ptr(bitset), _dev_ptr(neighbors),
                                                 _dev_ptr(distances)), "device search")
+
+
+    def search_device_no_alloc(self, queries, k, neighbors, distances, bitset=None, stream=0):
+        """Like search_device, but the library allocates no device memory (intermediate buffers
+        come from its fixed 32 MiB array); runs on `stream` and returns when the work is done."""
+        nq = int(queries.shape[0])
+        _check(lib().ovvsBruteForceSearchDeviceNoAlloc(self._res._h, self._h, _dev_ptr(queries),
+                                                       nq, k, _dev_ptr(bitset),
+                                                       _dev_ptr(neighbors), _dev_ptr(distances),
+                                                       c_void_p(int(stream))),
+               "device search without allocation")
 
 
 class neighbors:  # noqa: N801  (mirrors the reference's namespace class)

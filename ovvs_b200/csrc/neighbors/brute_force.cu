@@ -49,6 +49,15 @@ void plan_chunks(int dp, int* nchunk, int* cx, int* cw) {
   *nchunk = n;
 }
 
+}  // namespace
+
+int list_size_for(int64_t k_eff) {
+  const int64_t need = k_eff + std::max<int64_t>(2, (k_eff + 7) / 8);
+  for (int kl : {4, 8, 16, 32})
+    if (need <= kl) return kl;
+  return 0;
+}
+
 // Number of super-chunks per query tile: balances the per-CTA work of the statically strided
 // item schedule (every CTA runs items b, b + grid, ...) against the per-item overhead.
 int choose_num_sc(int num_qtiles, int num_dbtiles, int num_sms, int64_t cand_per_sc_bytes,
@@ -73,15 +82,6 @@ int choose_num_sc(int num_qtiles, int num_dbtiles, int num_sms, int64_t cand_per
   }
   *tiles_per_item = best_L;
   return best_sc;
-}
-
-}  // namespace
-
-int list_size_for(int64_t k_eff) {
-  const int64_t need = k_eff + std::max<int64_t>(2, (k_eff + 7) / 8);
-  for (int kl : {4, 8, 16, 32})
-    if (need <= kl) return kl;
-  return 0;
 }
 
 ovvsStatus build_from_device(rt::Resources& r, BruteIndex& ix, const void* d_data, int dtype,

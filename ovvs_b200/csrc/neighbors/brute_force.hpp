@@ -57,6 +57,11 @@ ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_
                          int64_t k, const uint8_t* d_bitset, int64_t* d_neighbors,
                          float* d_distances, int64_t* k_eff_out);
 
+// Number of super-chunks per query tile for the fused kernel's work items (items = query tiles x
+// super-chunks), limited so the candidate lists stay under cand_per_sc_bytes * sc <= 1.5 GB.
+int choose_num_sc(int num_qtiles, int num_dbtiles, int num_sms, int64_t cand_per_sc_bytes,
+                  int* tiles_per_item);
+
 // Candidate-list size the fused kernel uses for k_eff results (k_eff plus a re-rank margin),
 // 0 when k_eff is larger than the register lists support.
 int list_size_for(int64_t k_eff);
