@@ -195,132 +195,256 @@ ovvsStatus build_from_host(rt::Resources& r, BruteIndex& ix, const void* data, i
   return r.finish();
 }
 
-ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_queries, int64_t nq,
-                         int64_t k, const uint8_t* d_bitset, int64_t* d_neighbors,
-                         float* d_distances, int64_t* k_eff_out) {
-  cudaStream_t s = r.stream;
-  const int64_t k_eff = std::min<int64_t>(k, ix.n_total);
-  *k_eff_out = k_eff;
-  const int kl = list_size_for(k_eff);
-  if (kl == 0) return OVVS_STATUS_UNSUPPORTED;
-  if (ix.device != r.device) return OVVS_STATUS_INVALID_ARGUMENT;
-  const int64_t q_pad = (nq + kTileQ - 1) / kTileQ * kTileQ;
-  const int num_qtiles = static_cast<int>(q_pad / kTileQ);
-  const int dim = static_cast<int>(ix.dim);
+namespace {
 
-  r.mark(0);
+// Per-search state shared by the small-k and large-k paths.
+struct SearchCtx {
+  int64_t q_pad = 0;
+  int num_qtiles = 0;
   __half* a16 = nullptr;
-  float *q_mul = nullptr, *xn = nullptr;
+  float* q_mul = nullptr;
+  float* xn = nullptr;
   int* flag = nullptr;
-  OVVS_TRY(r.scratch(rt::kWsQueryA, static_cast<size_t>(q_pad) * 2 * ix.dp, &a16));
-  OVVS_TRY(r.scratch(rt::kWsQueryMul, q_pad, &q_mul));
-  OVVS_TRY(r.scratch(rt::kWsQueryNorm, q_pad, &xn));
-  OVVS_TRY(r.scratch(rt::kWsFlags, 4, &flag));
-  OVVS_TRY_CUDA(cudaMemsetAsync(flag, 0, sizeof(int), s));
-  prim::launch_query_prep(d_queries, nq, q_pad, dim, ix.dp, ix.metric, ix.e_db, a16, q_mul, xn,
-                          flag, s);
-  OVVS_TRY_CUDA(cudaGetLastError());
-
   uint32_t* allow = nullptr;
-  if (d_bitset) {
-    OVVS_TRY(r.scratch(rt::kWsAllow, ix.n_pad / 32, &allow));
-    prim::launch_allow_bits(d_bitset, ix.row_offset, ix.row_id.as<uint32_t>(), ix.n, ix.n_pad,
-                            allow, s);
-    OVVS_TRY_CUDA(cudaGetLastError());
-  }
+  prim::FusedMaps maps{};
+};
 
-  prim::FusedParams p{};
+// Fused-kernel parameters common to every launch of one search.
+ovvsStatus base_params(rt::Resources& r, const BruteIndex& ix, const SearchCtx& c, int64_t nq,
+                       prim::FusedParams* out) {
+  prim::FusedParams& p = *out;
+  p = prim::FusedParams{};
   p.dp = ix.dp;
   p.nchunk = ix.nchunk;
-  for (int c = 0; c < ix.nchunk; ++c) {
-    p.chunk_x[c] = ix.chunk_x[c];
-    p.chunk_w[c] = ix.chunk_w[c];
+  for (int i = 0; i < ix.nchunk; ++i) {
+    p.chunk_x[i] = ix.chunk_x[i];
+    p.chunk_w[i] = ix.chunk_w[i];
   }
   p.b_parts = ix.b_parts;
   p.nunits = ix.b_parts * ix.nchunk;
   if (!prim::plan_fused_smem(p, r.max_smem_optin)) return OVVS_STATUS_UNSUPPORTED;
   p.query_split = ix.metric != prim::kMetricHamming;
-  p.q_lo_flag = flag;
-  p.num_qtiles = num_qtiles;
+  p.q_lo_flag = c.flag;
+  p.num_qtiles = c.num_qtiles;
   p.num_dbtiles = ix.num_tiles;
-  const int64_t cand_per_sc = q_pad * kl * static_cast<int64_t>(sizeof(uint64_t));
-  p.num_sc = choose_num_sc(num_qtiles, ix.num_tiles, r.num_sms, cand_per_sc, &p.tiles_per_item);
-  p.num_items = num_qtiles * p.num_sc;
   p.n_rows = ix.n;
   p.row_aux = ix.aux.as<float>();
   p.tile_aux = ix.tile_aux.as<float2>();
   p.row_id = ix.row_id.as<uint32_t>();
-  p.q_mul = q_mul;
-  p.allow = allow;
+  p.q_mul = c.q_mul;
+  p.allow = c.allow;
   p.rank_kind = prim::rank_kind_of(ix.metric);
-  p.err = r.d_err;
-  uint64_t* cand = nullptr;
-  OVVS_TRY(r.scratch(rt::kWsCand, static_cast<size_t>(q_pad) * p.num_sc * kl, &cand));
-  p.out = cand;
-  uint64_t* bound = nullptr;
-  OVVS_TRY(r.scratch(rt::kWsBound, static_cast<size_t>(q_pad), &bound));
-  OVVS_TRY_CUDA(cudaMemsetAsync(bound, 0xFF, static_cast<size_t>(q_pad) * sizeof(uint64_t), s));
-  p.q_bound = bound;
   p.nq = nq;
-  p.k_pub = static_cast<int>(k_eff);
+  p.err = r.d_err;
+  return OVVS_STATUS_SUCCESS;
+}
 
-  prim::FusedMaps maps{};
-  const uint64_t a_cols = static_cast<uint64_t>(2 * ix.dp);
-  if (!rt::encode_f16_2d(&maps.a64, a16, a_cols, q_pad, 64, kTileQ) ||
-      !rt::encode_f16_2d(&maps.a32, a16, a_cols, q_pad, 32, kTileQ) ||
-      !rt::encode_f16_2d(&maps.a16, a16, a_cols, q_pad, 16, kTileQ)) {
-    return OVVS_STATUS_ERROR;
-  }
-  maps.b64 = ix.b64;
-  maps.b32 = ix.b32;
-  maps.b16 = ix.b16;
-  const int grid = static_cast<int>(std::min<int64_t>(p.num_items, r.num_sms));
-  r.mark(1);
-  OVVS_TRY_CUDA(prim::launch_knn_fused(maps, p, kl, grid, s));
-  r.mark(2);
-
+prim::MergeParams merge_params(const BruteIndex& ix, const SearchCtx& c, const float* d_queries,
+                               int64_t nq, int64_t k_eff) {
   prim::MergeParams m{};
-  m.cand = cand;
-  m.num_sc = p.num_sc;
-  m.kl = kl;
   m.nq = nq;
-  m.dim = dim;
+  m.dim = static_cast<int>(ix.dim);
   m.queries = d_queries;
-  m.xn = xn;
+  m.xn = c.xn;
   m.metric = ix.metric;
   m.exact32 = ix.exact32.get() ? ix.exact32.as<float>() : nullptr;
   m.rows16 = ix.rows16.as<__half>();
   m.rows16_stride = ix.b_parts * ix.dp;
   m.norm_sorted = ix.norm_sorted.as<float>();
   m.inv_perm = ix.inv_perm.as<uint32_t>();
-  m.allow = allow;
+  m.allow = c.allow;
   m.row_offset = ix.row_offset;
   m.k_eff = static_cast<int>(k_eff);
   m.negate_output = ix.metric == prim::kMetricInnerProduct;
-  if (!ix.sharded) {
+  return m;
+}
+
+int launch_grid(const prim::FusedParams& p, int num_sms) {
+  return static_cast<int>(std::min<int64_t>(p.num_items, num_sms));
+}
+
+// Large k (k plus re-rank margin above the register lists): bound pre-pass on a sample of the
+// tiles, append pass with that bound, then per-query sort + exact re-rank; repeated with a
+// tighter bound for queries whose buffer overflowed.
+ovvsStatus search_large(rt::Resources& r, const BruteIndex& ix, const SearchCtx& c,
+                        const float* d_queries, int64_t nq, int64_t k_eff, prim::MergeParams m) {
+  cudaStream_t s = r.stream;
+  const int margin = static_cast<int>(std::max<int64_t>(2, (k_eff + 7) / 8));
+  const int64_t need = k_eff + margin;
+  const bool prepass = ix.n > 4096;
+  int cap = 32;
+  const int64_t want = prepass ? 32 * need : std::max<int64_t>(ix.n, need);
+  while (cap < want && cap < prim::kSelectMaxCap) cap <<= 1;
+  if (need > cap) return OVVS_STATUS_UNSUPPORTED;  // k beyond ~7k rows per query
+
+  uint64_t* tau = nullptr;
+  uint32_t* count = nullptr;
+  uint64_t* buf = nullptr;
+  int* overflow = nullptr;
+  OVVS_TRY(r.scratch(rt::kWsBound, static_cast<size_t>(c.q_pad), &tau));
+  OVVS_TRY(r.scratch(rt::kWsAppCount, static_cast<size_t>(c.q_pad), &count));
+  OVVS_TRY(r.scratch(rt::kWsAppBuf, static_cast<size_t>(c.q_pad) * cap, &buf));
+  OVVS_TRY(r.scratch(rt::kWsOverflow, 1, &overflow));
+  OVVS_TRY_CUDA(cudaMemsetAsync(tau, 0xFF, static_cast<size_t>(c.q_pad) * sizeof(uint64_t), s));
+
+  if (prepass) {
+    // Lists of 32 over every stride-th tile; the need-th smallest key of their union bounds the
+    // need-th best key of the whole database (the union holds real rows).
+    const int stride = ix.num_tiles >= 64 ? 8 : 1;
+    const int sampled = (ix.num_tiles + stride - 1) / stride;
+    prim::FusedParams p;
+    OVVS_TRY(base_params(r, ix, c, nq, &p));
+    p.tile_stride = stride;
+    p.num_dbtiles = sampled;
+    const int64_t cand_per_sc = c.q_pad * 32 * static_cast<int64_t>(sizeof(uint64_t));
+    int num_sc = choose_num_sc(c.num_qtiles, sampled, r.num_sms, cand_per_sc, &p.tiles_per_item);
+    const int min_sc = static_cast<int>(std::min<int64_t>(sampled, (2 * need + 31) / 32));
+    if (num_sc < min_sc) {
+      p.tiles_per_item = (sampled + min_sc - 1) / min_sc;
+      num_sc = (sampled + p.tiles_per_item - 1) / p.tiles_per_item;
+    }
+    if (num_sc <= 256 && static_cast<int64_t>(num_sc) * 32 >= need) {
+      p.num_sc = num_sc;
+      p.num_items = c.num_qtiles * num_sc;
+      p.k_pub = 0;  // lists of 32 cannot bound rank `need`
+      uint64_t* cand = nullptr;
+      uint64_t* shared_bound = nullptr;
+      OVVS_TRY(r.scratch(rt::kWsCand, static_cast<size_t>(c.q_pad) * num_sc * 32, &cand));
+      OVVS_TRY(r.scratch(rt::kWsAppBound, static_cast<size_t>(c.q_pad), &shared_bound));
+      OVVS_TRY_CUDA(cudaMemsetAsync(shared_bound, 0xFF, static_cast<size_t>(c.q_pad) * 8, s));
+      p.q_bound = shared_bound;
+      p.out = cand;
+      OVVS_TRY_CUDA(prim::launch_knn_fused(c.maps, p, 32, launch_grid(p, r.num_sms), s));
+      OVVS_TRY_CUDA(prim::launch_kth_bound(cand, num_sc, nq, static_cast<int>(need), tau, s));
+    }
+  }
+
+  prim::FusedParams p;
+  OVVS_TRY(base_params(r, ix, c, nq, &p));
+  p.num_sc = choose_num_sc(c.num_qtiles, ix.num_tiles, r.num_sms, 0, &p.tiles_per_item);
+  p.num_items = c.num_qtiles * p.num_sc;
+  p.q_tau_key = tau;
+  p.app_count = count;
+  p.app_buf = buf;
+  p.app_cap = cap;
+  prim::SelectParams sp{};
+  sp.m = m;
+  sp.count = count;
+  sp.buf = buf;
+  sp.cap = cap;
+  sp.margin = margin;
+  sp.tau_key = tau;
+  sp.overflow = overflow;
+  constexpr int kMaxRounds = 16;
+  for (int round = 0; round < kMaxRounds; ++round) {
+    p.app_exact = round >= 2;  // persistent overflow: strict key bound (ties cannot pile up)
+    OVVS_TRY_CUDA(cudaMemsetAsync(count, 0, static_cast<size_t>(c.q_pad) * sizeof(uint32_t), s));
+    OVVS_TRY_CUDA(cudaMemsetAsync(overflow, 0, sizeof(int), s));
+    OVVS_TRY_CUDA(prim::launch_knn_fused(c.maps, p, 0, launch_grid(p, r.num_sms), s));
+    OVVS_TRY_CUDA(prim::launch_select_rerank(sp, s));
+    int host_overflow = 0;
+    OVVS_TRY_CUDA(cudaMemcpyAsync(&host_overflow, overflow, sizeof(int), cudaMemcpyDeviceToHost, s));
+    OVVS_TRY_CUDA(cudaStreamSynchronize(s));
+    if (!host_overflow) return OVVS_STATUS_SUCCESS;
+  }
+  return OVVS_STATUS_ERROR;
+}
+
+}  // namespace
+
+ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_queries, int64_t nq,
+                         int64_t k, const uint8_t* d_bitset, int64_t* d_neighbors,
+                         float* d_distances, int64_t* k_eff_out) {
+  cudaStream_t s = r.stream;
+  const int64_t k_eff = std::min<int64_t>(k, ix.n_total);
+  *k_eff_out = k_eff;
+  if (ix.device != r.device) return OVVS_STATUS_INVALID_ARGUMENT;
+  const int kl = list_size_for(k_eff);
+  const int dim = static_cast<int>(ix.dim);
+
+  SearchCtx c;
+  c.q_pad = (nq + kTileQ - 1) / kTileQ * kTileQ;
+  c.num_qtiles = static_cast<int>(c.q_pad / kTileQ);
+  r.mark(0);
+  OVVS_TRY(r.scratch(rt::kWsQueryA, static_cast<size_t>(c.q_pad) * 2 * ix.dp, &c.a16));
+  OVVS_TRY(r.scratch(rt::kWsQueryMul, c.q_pad, &c.q_mul));
+  OVVS_TRY(r.scratch(rt::kWsQueryNorm, c.q_pad, &c.xn));
+  OVVS_TRY(r.scratch(rt::kWsFlags, 4, &c.flag));
+  OVVS_TRY_CUDA(cudaMemsetAsync(c.flag, 0, sizeof(int), s));
+  prim::launch_query_prep(d_queries, nq, c.q_pad, dim, ix.dp, ix.metric, ix.e_db, c.a16, c.q_mul,
+                          c.xn, c.flag, s);
+  OVVS_TRY_CUDA(cudaGetLastError());
+  if (d_bitset) {
+    OVVS_TRY(r.scratch(rt::kWsAllow, ix.n_pad / 32, &c.allow));
+    prim::launch_allow_bits(d_bitset, ix.row_offset, ix.row_id.as<uint32_t>(), ix.n, ix.n_pad,
+                            c.allow, s);
+    OVVS_TRY_CUDA(cudaGetLastError());
+  }
+  const uint64_t a_cols = static_cast<uint64_t>(2 * ix.dp);
+  if (!rt::encode_f16_2d(&c.maps.a64, c.a16, a_cols, c.q_pad, 64, kTileQ) ||
+      !rt::encode_f16_2d(&c.maps.a32, c.a16, a_cols, c.q_pad, 32, kTileQ) ||
+      !rt::encode_f16_2d(&c.maps.a16, c.a16, a_cols, c.q_pad, 16, kTileQ)) {
+    return OVVS_STATUS_ERROR;
+  }
+  c.maps.b64 = ix.b64;
+  c.maps.b32 = ix.b32;
+  c.maps.b16 = ix.b16;
+
+  prim::MergeParams m = merge_params(ix, c, d_queries, nq, k_eff);
+  float *srank = nullptr, *grank = nullptr;
+  int64_t *sgid = nullptr, *ggid = nullptr;
+  const size_t cnt = static_cast<size_t>(nq) * k_eff;
+  if (ix.sharded) {
+    OVVS_TRY(r.scratch(rt::kWsShardRank, cnt, &srank));
+    OVVS_TRY(r.scratch(rt::kWsShardGid, cnt, &sgid));
+    OVVS_TRY(r.scratch(rt::kWsGatherRank, cnt * r.world, &grank));
+    OVVS_TRY(r.scratch(rt::kWsGatherGid, cnt * r.world, &ggid));
+    m.shard_rank = srank;
+    m.shard_gid = sgid;
+  } else {
     m.neighbors = d_neighbors;
     m.distances = d_distances;
+  }
+
+  if (kl == 0) {
+    r.mark(1);
+    OVVS_TRY(search_large(r, ix, c, d_queries, nq, k_eff, m));
+    r.mark(2);
+    r.mark(3);
+  } else {
+    prim::FusedParams p;
+    OVVS_TRY(base_params(r, ix, c, nq, &p));
+    const int64_t cand_per_sc = c.q_pad * kl * static_cast<int64_t>(sizeof(uint64_t));
+    p.num_sc = choose_num_sc(c.num_qtiles, ix.num_tiles, r.num_sms, cand_per_sc,
+                             &p.tiles_per_item);
+    p.num_items = c.num_qtiles * p.num_sc;
+    uint64_t* cand = nullptr;
+    OVVS_TRY(r.scratch(rt::kWsCand, static_cast<size_t>(c.q_pad) * p.num_sc * kl, &cand));
+    p.out = cand;
+    uint64_t* bound = nullptr;
+    OVVS_TRY(r.scratch(rt::kWsBound, static_cast<size_t>(c.q_pad), &bound));
+    OVVS_TRY_CUDA(cudaMemsetAsync(bound, 0xFF, static_cast<size_t>(c.q_pad) * sizeof(uint64_t), s));
+    p.q_bound = bound;
+    p.k_pub = static_cast<int>(k_eff);
+    r.mark(1);
+    OVVS_TRY_CUDA(prim::launch_knn_fused(c.maps, p, kl, launch_grid(p, r.num_sms), s));
+    r.mark(2);
+    m.cand = cand;
+    m.num_sc = p.num_sc;
+    m.kl = kl;
     OVVS_TRY_CUDA(prim::launch_merge_rerank(m, s));
     r.mark(3);
+  }
+  if (!ix.sharded) {
     r.mark(4);
     return OVVS_STATUS_SUCCESS;
   }
   // Sharded: exact per-shard top-k, all-gather over NVLink, then an exact (rank, id) merge.
-  const size_t cnt = static_cast<size_t>(nq) * k_eff;
-  float *srank = nullptr, *grank = nullptr;
-  int64_t *sgid = nullptr, *ggid = nullptr;
-  OVVS_TRY(r.scratch(rt::kWsShardRank, cnt, &srank));
-  OVVS_TRY(r.scratch(rt::kWsShardGid, cnt, &sgid));
-  OVVS_TRY(r.scratch(rt::kWsGatherRank, cnt * r.world, &grank));
-  OVVS_TRY(r.scratch(rt::kWsGatherGid, cnt * r.world, &ggid));
-  m.shard_rank = srank;
-  m.shard_gid = sgid;
-  OVVS_TRY_CUDA(prim::launch_merge_rerank(m, s));
-  r.mark(3);
-  OVVS_TRY(rt::status_of(ovvs::rt::nccl()->GroupStart()));
-  OVVS_TRY(rt::status_of(ovvs::rt::nccl()->AllGather(srank, grank, cnt, ncclFloat32, r.comm, s)));
-  OVVS_TRY(rt::status_of(ovvs::rt::nccl()->AllGather(sgid, ggid, cnt, ncclInt64, r.comm, s)));
-  OVVS_TRY(rt::status_of(ovvs::rt::nccl()->GroupEnd()));
+  const rt::NcclApi* nc = rt::nccl();
+  OVVS_TRY(rt::status_of(nc->GroupStart()));
+  OVVS_TRY(rt::status_of(nc->AllGather(srank, grank, cnt, ncclFloat32, r.comm, s)));
+  OVVS_TRY(rt::status_of(nc->AllGather(sgid, ggid, cnt, ncclInt64, r.comm, s)));
+  OVVS_TRY(rt::status_of(nc->GroupEnd()));
   OVVS_TRY_CUDA(prim::launch_shard_merge(grank, ggid, r.world, nq, static_cast<int>(k_eff),
                                          m.negate_output, d_neighbors, d_distances, s));
   r.mark(4);

@@ -114,7 +114,7 @@ __device__ void run_producer(const FusedParams& p, const FusedMaps& maps, const 
         ptx::mbar_arrive_expect_tx(&s.full[slot], static_cast<uint32_t>(kTileN * w * 2));
         ptx::tma_load_2d(s.base + p.stage_off + slot * kUnitBytes,
                          pick_map(w, &maps.b64, &maps.b32, &maps.b16), bp * p.dp + p.chunk_x[c],
-                         t * kTileN, &s.full[slot]);
+                         t * p.tile_stride * kTileN, &s.full[slot]);
         ++unit;
       }
     }
@@ -255,12 +255,15 @@ __device__ __forceinline__ float max32(const float (&r)[32]) {
 
 template <int KL>
 struct EpiState {
-  uint64_t L[KL];
+  uint64_t L[KL > 0 ? KL : 1];
   float m;
   float thr;      // s-space threshold for the current tile
   float gw;       // ranking value of the shared per-query bound (+ slack), NaN when none
   float2 ta;
   bool real;      // this lane holds a real query
+  int64_t qi;     // this lane's query index
+  uint64_t gkey;  // append mode: the query's bound key
+  bool by_key;    // append mode: compare keys (bound value not finite, or exact mode)
 };
 
 // Ranking value the filter compares against: the list's own worst entry, tightened by the
@@ -273,8 +276,18 @@ __device__ __forceinline__ void refresh_threshold(EpiState<KL>& st, int kind) {
     st.thr = kInf;  // padding lanes never select
     return;
   }
-  const float own = keys::key_value(st.L[KL - 1]);  // NaN while the list is not full
-  st.thr = s_threshold(fminf(own, st.gw), st.m, st.ta, kind);
+  if constexpr (KL == 0) {  // append mode: fixed per-query threshold (already has its slack)
+    st.thr = s_threshold(st.gw, st.m, st.ta, kind);
+  } else {
+    const float own = keys::key_value(st.L[KL - 1]);  // NaN while the list is not full
+    st.thr = s_threshold(fminf(own, st.gw), st.m, st.ta, kind);
+  }
+}
+
+// Append-mode threshold in ranking-value space: the bound value plus a relative slack of 1e-5.
+__device__ __forceinline__ float append_limit(float tau, float2 ta) {
+  if (!(tau < kInf)) return tau;
+  return tau + (fabsf(tau) + fabsf(ta.x) + fabsf(ta.y)) * 1e-5f;
 }
 
 template <int KL>
@@ -288,6 +301,7 @@ __device__ __forceinline__ void read_bound(const FusedParams& p, int64_t q, EpiS
 template <int KL>
 __device__ __forceinline__ void publish_bound(const FusedParams& p, int64_t q,
                                               const EpiState<KL>& st) {
+  if (p.k_pub < 1 || p.k_pub > KL) return;  // the list cannot bound that rank
   // Branch-free selection keeps the list in registers (a select chain would be turned into an
   // indexed load, which moves the whole list to local memory).
   uint64_t kth = 0;
@@ -326,9 +340,17 @@ __device__ __forceinline__ void slow_path(const FusedParams& p, const float (&r)
       v = sv * p.row_aux[pos];
     }
     const uint64_t key = keys::make_key(v, p.row_id[pos]);
-    if (key < st.L[KL - 1]) {
-      list_insert<KL>(st.L, key);
-      refresh_threshold<KL>(st, p.rank_kind);
+    if constexpr (KL == 0) {
+      if (st.by_key ? key <= st.gkey : v <= st.gw) {
+        const uint32_t slot = atomicAdd(p.app_count + st.qi, 1u);
+        if (slot < static_cast<uint32_t>(p.app_cap))
+          p.app_buf[static_cast<size_t>(st.qi) * p.app_cap + slot] = key;
+      }
+    } else {
+      if (key < st.L[KL - 1]) {
+        list_insert<KL>(st.L, key);
+        refresh_threshold<KL>(st, p.rank_kind);
+      }
     }
   }
 }
@@ -352,10 +374,15 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
     const int64_t q = static_cast<int64_t>(it.qt) * kTileQ + warp * 32 + lane;
     st.m = p.q_mul[q];
     st.real = q < p.nq;
-    st.ta = p.tile_aux[it.t0];
-    read_bound<KL>(p, q, st);
+    st.qi = q;
+    st.ta = p.tile_aux[it.t0 * p.tile_stride];
+    if constexpr (KL > 0) {
+      read_bound<KL>(p, q, st);
 #pragma unroll
-    for (int i = 0; i < KL; ++i) st.L[i] = kEmptyKey;
+      for (int i = 0; i < KL; ++i) st.L[i] = kEmptyKey;
+    } else {
+      st.gkey = p.q_tau_key[q];
+    }
     bool ok = true;
     for (int t = it.t0; t < it.t1; ++t) {
       const uint32_t buf = tile & 1, use = tile >> 1;
@@ -367,14 +394,21 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
         break;
       }
       ptx::tc_fence_after();
-      st.ta = p.tile_aux[t];
-      if (((t - it.t0) & (kBoundPeriod - 1)) == kBoundPeriod - 1 && st.real) {
-        publish_bound<KL>(p, q, st);
-        read_bound<KL>(p, q, st);
+      const int tile_pos = t * p.tile_stride;
+      st.ta = p.tile_aux[tile_pos];
+      if constexpr (KL > 0) {
+        if (((t - it.t0) & (kBoundPeriod - 1)) == kBoundPeriod - 1 && st.real) {
+          publish_bound<KL>(p, q, st);
+          read_bound<KL>(p, q, st);
+        }
+      } else {
+        const float tv = keys::key_value(st.gkey);
+        st.by_key = p.app_exact || !(tv < kInf);
+        st.gw = st.by_key ? tv : append_limit(tv, st.ta);
       }
       refresh_threshold<KL>(st, p.rank_kind);
       const uint32_t taddr = lane_base + buf * kTileN;
-      const int64_t col_base = static_cast<int64_t>(t) * kTileN;
+      const int64_t col_base = static_cast<int64_t>(tile_pos) * kTileN;
       float ra[32], rb[32];
       ptx::tmem_ld32(taddr, ra);
       ptx::tmem_wait_ld();
@@ -399,10 +433,12 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
       ++tile;
     }
     if (!ok) return;
-    if (st.real) publish_bound<KL>(p, q, st);
-    uint64_t* dst = p.out + (static_cast<size_t>(q) * p.num_sc + it.sc) * KL;
+    if constexpr (KL > 0) {
+      if (st.real) publish_bound<KL>(p, q, st);
+      uint64_t* dst = p.out + (static_cast<size_t>(q) * p.num_sc + it.sc) * KL;
 #pragma unroll
-    for (int i = 0; i < KL; ++i) dst[i] = st.L[i];
+      for (int i = 0; i < KL; ++i) dst[i] = st.L[i];
+    }
   }
 }
 
@@ -506,6 +542,8 @@ cudaError_t launch_knn_fused(const FusedMaps& maps, const FusedParams& p, int kl
       return launch_kl<16>(maps, p, grid, stream);
     case 32:
       return launch_kl<32>(maps, p, grid, stream);
+    case 0:
+      return launch_kl<0>(maps, p, grid, stream);
     default:
       return cudaErrorInvalidValue;
   }

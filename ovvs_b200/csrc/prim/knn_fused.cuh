@@ -87,8 +87,19 @@ struct FusedParams {
   int64_t nq;                      // real queries (lanes >= nq are padding and never select)
   int k_pub;                       // rank (1-based) whose key a list publishes as a bound
   uint64_t* q_bound;               // [q_pad] smallest published k_pub-th key per query
-  uint64_t* out;                   // [q_pad][num_sc][KL] sorted keys
+  uint64_t* out;                   // [q_pad][num_sc][KL] sorted keys (list mode)
   int* err;                        // watchdog word
+  int tile_stride = 1;             // item tile ranges count every tile_stride-th database tile
+  // Append mode (KL = 0): every column whose key is within the query's bound q_tau_key[q] is
+  // appended to the query's buffer app_buf[q * app_cap + i]; app_count[q] counts them (it may
+  // exceed app_cap: the caller then tightens the bound and runs again). With a finite bound value
+  // the test is value <= bound value (+ relative slack 1e-5, so near-ties survive for the exact
+  // re-rank); otherwise, or with app_exact, it is key <= bound key (kEmptyKey keeps everything).
+  const uint64_t* q_tau_key;
+  int app_exact;
+  uint32_t* app_count;
+  uint64_t* app_buf;
+  int app_cap;
 };
 
 // Every kBoundPeriod tiles each epilogue thread publishes its list's k_pub-th key to q_bound
@@ -102,7 +113,8 @@ struct FusedMaps {
   CUtensorMap b64, b32, b16;  // rows    [n_pad, b_parts * dp] fp16, boxes {64|32|16, 256}
 };
 
-// Host-side launcher (knn_fused.cu). `kl` in {4, 8, 16, 32}.
+// Host-side launcher (knn_fused.cu). `kl` in {4, 8, 16, 32} (sorted register lists), or 0 for
+// append mode.
 cudaError_t launch_knn_fused(const FusedMaps& maps, const FusedParams& p, int kl, int grid,
                              cudaStream_t stream);
 

@@ -202,6 +202,131 @@ __global__ void shard_merge_kernel(const float* __restrict__ rank, const int64_t
   }
 }
 
+__global__ void kth_bound_kernel(const uint64_t* __restrict__ cand, int num_sc, int64_t nq,
+                                 int k, uint64_t* __restrict__ tau_key) {
+  constexpr int KL = 32;
+  const int lane = threadIdx.x & 31;
+  const int64_t q = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (q >= nq) return;
+  const uint64_t* c = cand + static_cast<size_t>(q) * num_sc * KL;
+  // lane l walks lists l, l+32, ...: its head is the smallest unconsumed key among them
+  int ptr[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  const int mine = (num_sc - lane + 31) / 32;  // lists owned by this lane (<= 8: num_sc <= 256)
+  uint64_t kth = kEmptyKey;
+  for (int r = 0; r < k; ++r) {
+    uint64_t head = kEmptyKey;
+    int which = -1;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j < mine && ptr[j] < KL) {
+        const uint64_t v = c[(lane + 32 * j) * KL + ptr[j]];
+        if (v < head) {
+          head = v;
+          which = j;
+        }
+      }
+    }
+    uint64_t best = head;
+    int bl = lane;
+    warp_argmin(best, bl);
+    if (best == kEmptyKey) {
+      kth = kEmptyKey;
+      break;
+    }
+    if (lane == bl) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j == which) ++ptr[j];
+    }
+    kth = best;
+  }
+  if (lane == 0) tau_key[q] = kth;
+}
+
+__device__ __forceinline__ void bitonic_block(uint64_t* key, float* val, int n) {
+  // Ascending bitonic sort of n (power of two) entries in shared memory by the whole block.
+  for (int size = 2; size <= n; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      __syncthreads();
+      for (int i = threadIdx.x; i < n / 2; i += blockDim.x) {
+        const int lo = 2 * i - (i & (stride - 1));
+        const int hi = lo + stride;
+        const bool up = (lo & size) == 0;
+        const uint64_t a = key[lo], b = key[hi];
+        if ((a > b) == up) {
+          key[lo] = b;
+          key[hi] = a;
+          if (val) {
+            const float t = val[lo];
+            val[lo] = val[hi];
+            val[hi] = t;
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(256) select_rerank_kernel(const SelectParams sp) {
+  extern __shared__ uint64_t sel_smem[];
+  const MergeParams& p = sp.m;
+  const int64_t q = blockIdx.x;
+  if (q >= p.nq) return;
+  uint64_t* cand = sel_smem;                                    // [cap] buffered keys
+  uint64_t* ekey = sel_smem + sp.cap;                           // [cap] exact keys
+  float* erank = reinterpret_cast<float*>(sel_smem + 2 * sp.cap);  // [cap] exact ranking values
+  const uint32_t cnt = sp.count[q];
+  const int n = static_cast<int>(cnt < static_cast<uint32_t>(sp.cap) ? cnt : static_cast<uint32_t>(sp.cap));
+  int P = 32;
+  while (P < n) P <<= 1;
+  const uint64_t* b = sp.buf + static_cast<size_t>(q) * sp.cap;
+  for (int i = threadIdx.x; i < P; i += blockDim.x) cand[i] = i < n ? b[i] : kEmptyKey;
+  bitonic_block(cand, nullptr, P);
+  const int T = min(n, p.k_eff + sp.margin);
+  if (cnt > static_cast<uint32_t>(sp.cap)) {
+    // The buffer holds cap real rows, so its T-th key bounds the T-th best of the database.
+    if (threadIdx.x == 0) {
+      sp.tau_key[q] = cand[T - 1];
+      atomicOr(sp.overflow, 1);
+    }
+    return;
+  }
+  // Exact re-rank of the T best candidates.
+  const float* x = p.queries + q * p.dim;
+  const float xn = p.xn[q];
+  int P2 = 32;
+  while (P2 < T) P2 <<= 1;
+  for (int i = threadIdx.x; i < P2; i += blockDim.x) {
+    uint64_t ek = kEmptyKey;
+    float rank = __int_as_float(0x7fffffff);
+    if (i < T && cand[i] != kEmptyKey) {
+      const uint32_t id = keys::key_id(cand[i]);
+      const int64_t pos = p.inv_perm[id];
+      const bool allowed = p.allow == nullptr || ((p.allow[pos >> 5] >> (pos & 31)) & 1u);
+      rank = allowed ? exact_rank(p, x, xn, pos) : __int_as_float(0x7f800000);
+      ek = keys::make_key(rank, id);
+    }
+    ekey[i] = ek;
+    erank[i] = rank;
+  }
+  bitonic_block(ekey, erank, P2);
+  for (int i = threadIdx.x; i < p.k_eff; i += blockDim.x) {
+    const size_t o = static_cast<size_t>(q) * p.k_eff + i;
+    const uint64_t key = i < P2 ? ekey[i] : kEmptyKey;
+    const float rank = i < P2 ? erank[i] : __int_as_float(0x7fffffff);
+    const bool empty = key == kEmptyKey;
+    const int64_t gid = p.row_offset + static_cast<int64_t>(keys::key_id(key));
+    if (p.neighbors) {
+      p.neighbors[o] = empty ? -1 : gid;
+      p.distances[o] = p.negate_output ? -rank : rank;
+    } else {
+      p.shard_rank[o] = rank;
+      p.shard_gid[o] = empty ? INT64_MAX : gid;
+    }
+  }
+}
+
 template <int KL>
 cudaError_t launch_kl(const MergeParams& p, cudaStream_t stream) {
   const size_t smem = static_cast<size_t>(kMergeWarps) * 32 * KL * sizeof(uint64_t);
@@ -231,6 +356,27 @@ cudaError_t launch_merge_rerank(const MergeParams& p, cudaStream_t stream) {
     default:
       return cudaErrorInvalidValue;
   }
+}
+
+cudaError_t launch_kth_bound(const uint64_t* cand, int num_sc, int64_t nq, int k,
+                             uint64_t* tau_key, cudaStream_t stream) {
+  if (num_sc > 256) return cudaErrorInvalidValue;
+  const int wpb = 8;
+  const int64_t blocks = (nq + wpb - 1) / wpb;
+  kth_bound_kernel<<<static_cast<unsigned>(blocks), wpb * 32, 0, stream>>>(cand, num_sc, nq, k,
+                                                                        tau_key);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_select_rerank(const SelectParams& p, cudaStream_t stream) {
+  if (p.cap > kSelectMaxCap || (p.cap & (p.cap - 1)) != 0) return cudaErrorInvalidValue;
+  const size_t smem = static_cast<size_t>(p.cap) * (2 * sizeof(uint64_t) + sizeof(float));
+  cudaError_t e = cudaFuncSetAttribute(select_rerank_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  select_rerank_kernel<<<static_cast<unsigned>(p.m.nq), 256, smem, stream>>>(p);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_shard_merge(const float* rank, const int64_t* gid, int world, int64_t nq,

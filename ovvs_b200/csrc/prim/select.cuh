@@ -43,6 +43,28 @@ struct MergeParams {
 
 cudaError_t launch_merge_rerank(const MergeParams& p, cudaStream_t stream);
 
+// Large k. tau_key[q] = the k-th smallest key of the union of the num_sc sorted lists of 32 keys
+// in cand (kEmptyKey when the union has fewer than k keys): an upper bound on the k-th best key
+// of the whole database, since the union holds real rows.
+cudaError_t launch_kth_bound(const uint64_t* cand, int num_sc, int64_t nq, int k,
+                             uint64_t* tau_key, cudaStream_t stream);
+
+// Large k. For each query the append buffer app_buf[q*cap, q*cap + min(count, cap)) is sorted,
+// its best min(count, k_eff + margin) keys are re-ranked exactly and k_eff results written (as in
+// MergeParams). A query whose count exceeded cap gets tau_key[q] = its buffer's (k_eff+margin)-th
+// key (a tighter bound) and sets *overflow; the caller re-runs the append pass.
+struct SelectParams {
+  MergeParams m;              // cand / num_sc / kl unused
+  const uint32_t* count;
+  const uint64_t* buf;
+  int cap;                    // power of two, <= kSelectMaxCap
+  int margin;
+  uint64_t* tau_key;
+  int* overflow;
+};
+constexpr int kSelectMaxCap = 8192;
+cudaError_t launch_select_rerank(const SelectParams& p, cudaStream_t stream);
+
 // Cross-shard merge after the all-gather: rank/gid are [world][nq][k_eff]; each shard's list is
 // sorted. Writes neighbors/distances [nq][k_eff] ordered by (rank, global id), NaN last.
 cudaError_t launch_shard_merge(const float* rank, const int64_t* gid, int world, int64_t nq,

@@ -72,7 +72,11 @@ enum WorkSlot : int {
   kWsBitset,       // caller bitset (host searches)
   kWsAllow,        // position-ordered allow bits
   kWsCand,         // fused-kernel candidate lists
-  kWsBound,        // shared per-query bound of the fused kernel
+  kWsBound,        // shared per-query bound of the fused kernel / large-k bound keys
+  kWsAppCount,     // large k: per-query append counts
+  kWsAppBuf,       // large k: per-query append buffers
+  kWsAppBound,     // large k: shared bound of the pre-pass lists
+  kWsOverflow,     // large k: append-buffer overflow flag
   kWsNeighbors,    // results (host searches)
   kWsDistances,
   kWsShardRank,    // per-shard results for the all-gather

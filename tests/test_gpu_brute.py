@@ -228,3 +228,42 @@ def test_second_resources_same_index(ovvs, gpu, oracle):
     for i in range(4):
         rnb, rds = oracle.brute_search(data, qs[i], 5, "l2")
         assert_search_equal(results[i][0], results[i][1], rnb, rds, what=f"thread {i}")
+
+
+@pytest.mark.parametrize("k", [29, 32, 64, 100, 256, 1000])
+def test_large_k(k, ovvs, gpu, oracle):
+    """k + margin beyond the register lists: bound pre-pass + append buffers + exact select."""
+    _run_parity(ovvs, gpu, oracle, "inner_product", "f32", n=40000, dim=48, nq=150, k=k, seed=k,
+                kind="unit")
+
+
+@pytest.mark.parametrize("metric", ["l2", "cosine"])
+def test_large_k_l2_cosine_mixture(metric, ovvs, gpu, oracle):
+    _run_parity(ovvs, gpu, oracle, metric, "f16", n=60000, dim=64, nq=130, k=100, seed=3,
+                kind="mixture", fp16_queries=True)
+
+
+def test_large_k_small_n_and_bitset(ovvs, gpu, oracle):
+    rng = np.random.default_rng(8)
+    n = 3000  # no pre-pass: every row is appended
+    ids = np.nonzero(rng.random(n) < 0.3)[0]
+    bs = ovvs.bitset_from_allow_list(n, ids)
+    _run_parity(ovvs, gpu, oracle, "l2", "f32", n=n, dim=20, nq=40, k=200, seed=8, bitset=bs)
+    few = ovvs.bitset_from_allow_list(n, ids[:50])  # fewer allowed rows than k
+    _run_parity(ovvs, gpu, oracle, "inner_product", "f32", n=n, dim=20, nq=40, k=120, seed=9,
+                bitset=few)
+
+
+def test_large_k_overflow_retry(ovvs, gpu, oracle):
+    """Thousands of exact duplicates at the cut-off overflow the append buffers; the bound is
+    tightened (finally on keys) until every query fits, and ties still resolve by lower id."""
+    rng = np.random.default_rng(10)
+    base = rng.standard_normal((4, 24)).astype(np.float32)
+    data = np.vstack([base[rng.integers(0, 4, 30000)],
+                      rng.standard_normal((20000, 24)).astype(np.float32) * 3])
+    q = base + 0.001
+    ix = ovvs.BruteIndex.build(data, resources=gpu)
+    nb, ds = ix.search(q, k=100)
+    rnb, rds = oracle.brute_search(data, q, 100, "l2")
+    assert_search_equal(nb, ds, rnb, rds, what="overflow retry")
+    ix.close()
