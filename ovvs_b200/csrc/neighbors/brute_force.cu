@@ -296,26 +296,30 @@ ovvsStatus search_large(rt::Resources& r, const BruteIndex& ix, const SearchCtx&
     OVVS_TRY(base_params(r, ix, c, nq, &p));
     p.tile_stride = stride;
     p.num_dbtiles = sampled;
-    const int64_t cand_per_sc = c.q_pad * 32 * static_cast<int64_t>(sizeof(uint64_t));
+    const int64_t cand_per_sc =
+        c.q_pad * 32 * prim::kListsPerItem * static_cast<int64_t>(sizeof(uint64_t));
     int num_sc = choose_num_sc(c.num_qtiles, sampled, r.num_sms, cand_per_sc, &p.tiles_per_item);
-    const int min_sc = static_cast<int>(std::min<int64_t>(sampled, (2 * need + 31) / 32));
+    const int min_sc = static_cast<int>(
+        std::min<int64_t>(sampled, (2 * need + 32 * prim::kListsPerItem - 1) /
+                                       (32 * prim::kListsPerItem)));
     if (num_sc < min_sc) {
       p.tiles_per_item = (sampled + min_sc - 1) / min_sc;
       num_sc = (sampled + p.tiles_per_item - 1) / p.tiles_per_item;
     }
-    if (num_sc <= 256 && static_cast<int64_t>(num_sc) * 32 >= need) {
+    const int lists = num_sc * prim::kListsPerItem;
+    if (lists <= 256 && static_cast<int64_t>(lists) * 32 >= need) {
       p.num_sc = num_sc;
       p.num_items = c.num_qtiles * num_sc;
       p.k_pub = 0;  // lists of 32 cannot bound rank `need`
       uint64_t* cand = nullptr;
       uint64_t* shared_bound = nullptr;
-      OVVS_TRY(r.scratch(rt::kWsCand, static_cast<size_t>(c.q_pad) * num_sc * 32, &cand));
+      OVVS_TRY(r.scratch(rt::kWsCand, static_cast<size_t>(c.q_pad) * lists * 32, &cand));
       OVVS_TRY(r.scratch(rt::kWsAppBound, static_cast<size_t>(c.q_pad), &shared_bound));
       OVVS_TRY_CUDA(cudaMemsetAsync(shared_bound, 0xFF, static_cast<size_t>(c.q_pad) * 8, s));
       p.q_bound = shared_bound;
       p.out = cand;
       OVVS_TRY_CUDA(prim::launch_knn_fused(c.maps, p, 32, launch_grid(p, r.num_sms), s));
-      OVVS_TRY_CUDA(prim::launch_kth_bound(cand, num_sc, nq, static_cast<int>(need), tau, s));
+      OVVS_TRY_CUDA(prim::launch_kth_bound(cand, lists, nq, static_cast<int>(need), tau, s));
     }
   }
 
@@ -414,12 +418,14 @@ ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_
   } else {
     prim::FusedParams p;
     OVVS_TRY(base_params(r, ix, c, nq, &p));
-    const int64_t cand_per_sc = c.q_pad * kl * static_cast<int64_t>(sizeof(uint64_t));
+    const int64_t cand_per_sc =
+        c.q_pad * kl * prim::kListsPerItem * static_cast<int64_t>(sizeof(uint64_t));
     p.num_sc = choose_num_sc(c.num_qtiles, ix.num_tiles, r.num_sms, cand_per_sc,
                              &p.tiles_per_item);
     p.num_items = c.num_qtiles * p.num_sc;
     uint64_t* cand = nullptr;
-    OVVS_TRY(r.scratch(rt::kWsCand, static_cast<size_t>(c.q_pad) * p.num_sc * kl, &cand));
+    OVVS_TRY(r.scratch(rt::kWsCand,
+                       static_cast<size_t>(c.q_pad) * p.num_sc * prim::kListsPerItem * kl, &cand));
     p.out = cand;
     uint64_t* bound = nullptr;
     OVVS_TRY(r.scratch(rt::kWsBound, static_cast<size_t>(c.q_pad), &bound));
@@ -430,7 +436,7 @@ ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_
     OVVS_TRY_CUDA(prim::launch_knn_fused(c.maps, p, kl, launch_grid(p, r.num_sms), s));
     r.mark(2);
     m.cand = cand;
-    m.num_sc = p.num_sc;
+    m.num_sc = p.num_sc * prim::kListsPerItem;  // lists per query
     m.kl = kl;
     OVVS_TRY_CUDA(prim::launch_merge_rerank(m, s));
     r.mark(3);

@@ -110,7 +110,7 @@ extern "C" ovvsStatus ovvsBruteForceSearchDeviceNoAlloc(ovvsResources_t res,
                        2 * piece(static_cast<size_t>(q_pad) * sizeof(float)) +
                        piece(static_cast<size_t>(q_pad) * sizeof(uint64_t)) +
                        (d_bitset ? piece(static_cast<size_t>(ix.n_pad / 32) * sizeof(uint32_t)) : 0);
-  const size_t cand_per_sc = static_cast<size_t>(q_pad) * kl * sizeof(uint64_t);
+  const size_t cand_per_sc = static_cast<size_t>(q_pad) * kl * prim::kListsPerItem * sizeof(uint64_t);
   if (fixed + piece(cand_per_sc) > kNoAllocScratchBytes) return OVVS_STATUS_SHAPE_MISMATCH;
   const size_t cand_budget = kNoAllocScratchBytes - fixed - 256;
 
@@ -188,7 +188,7 @@ extern "C" ovvsStatus ovvsBruteForceSearchDeviceNoAlloc(ovvsResources_t res,
 
   prim::MergeParams m{};
   m.cand = cand;
-  m.num_sc = p.num_sc;
+  m.num_sc = p.num_sc * prim::kListsPerItem;  // lists per query
   m.kl = kl;
   m.nq = nq;
   m.dim = dim;

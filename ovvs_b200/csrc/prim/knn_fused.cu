@@ -17,7 +17,7 @@ struct Smem {
   uint64_t* full;    // [nstages] TMA -> MMA
   uint64_t* empty;   // [nstages] MMA -> TMA
   uint64_t* tfull;   // [2] MMA -> epilogue
-  uint64_t* tempty;  // [2] epilogue -> MMA (4 arrivals: one per epilogue warp)
+  uint64_t* tempty;  // [2] epilogue -> MMA (one arrival per epilogue warp)
   uint64_t* afull;   // query tile landed
   uint64_t* aempty;  // MMA done with the query tile
   uint64_t* drain;   // final MMA completion
@@ -310,21 +310,33 @@ __device__ __forceinline__ void publish_bound(const FusedParams& p, int64_t q,
   if (kth != kEmptyKey) atomicMin(reinterpret_cast<unsigned long long*>(p.q_bound + q), kth);
 }
 
+// r[j] for a run-time j through a tree of selects on statically indexed registers (an indexed
+// access would move the array to local memory).
+__device__ __forceinline__ float pick32(const float (&r)[32], int j) {
+  float a[16], b[8], c[4], d[2];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) a[i] = (j & 16) ? r[i + 16] : r[i];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) b[i] = (j & 8) ? a[i + 8] : a[i];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) c[i] = (j & 4) ? b[i + 4] : b[i];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) d[i] = (j & 2) ? c[i + 2] : c[i];
+  return (j & 1) ? d[1] : d[0];
+}
+
 template <int KL>
 __device__ __forceinline__ void slow_path(const FusedParams& p, const float (&r)[32],
-                                          float* scratch, int64_t col0, EpiState<KL>& st) {
+                                          int64_t col0, EpiState<KL>& st) {
   // Visit only the columns that pass the conservative bound (NaN passes: its exact key is
   // decided below).
   uint32_t mask = 0;
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    mask |= static_cast<uint32_t>(!(r[j] < st.thr)) << j;
-    scratch[j] = r[j];
-  }
+  for (int j = 0; j < 32; ++j) mask |= static_cast<uint32_t>(!(r[j] < st.thr)) << j;
   while (mask) {
     const int j = __ffs(mask) - 1;
     mask &= mask - 1;
-    const float sv = scratch[j];
+    const float sv = pick32(r, j);
     if (sv < st.thr) continue;  // threshold tightened by an earlier insertion
     const int64_t pos = col0 + j;
     if (pos >= p.n_rows) break;
@@ -357,21 +369,22 @@ __device__ __forceinline__ void slow_path(const FusedParams& p, const float (&r)
 
 template <int KL>
 __device__ __forceinline__ void process_chunk(const FusedParams& p, const float (&r)[32],
-                                              float* scratch, int64_t col0, EpiState<KL>& st) {
+                                              int64_t col0, EpiState<KL>& st) {
   const float g = max32(r);
-  if (!(g < st.thr)) slow_path<KL>(p, r, scratch, col0, st);
+  if (!(g < st.thr)) slow_path<KL>(p, r, col0, st);
+  __syncwarp();  // tcgen05.ld / wait::ld are warp-collective: reconverge after the slow path
 }
 
 template <int KL>
 __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_base) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* scratch = reinterpret_cast<float*>(s.base + p.scratch_off) + threadIdx.x * kScratchStride;
-  const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
+  const int quarter = warp & 3, half = warp >> 2;
+  const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
   uint32_t tile = 0;
   EpiState<KL> st;
   for (int item = blockIdx.x; item < p.num_items; item += gridDim.x) {
     const Item it = item_of(p, item);
-    const int64_t q = static_cast<int64_t>(it.qt) * kTileQ + warp * 32 + lane;
+    const int64_t q = static_cast<int64_t>(it.qt) * kTileQ + quarter * 32 + lane;
     st.m = p.q_mul[q];
     st.real = q < p.nq;
     st.qi = q;
@@ -407,35 +420,50 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
         st.gw = st.by_key ? tv : append_limit(tv, st.ta);
       }
       refresh_threshold<KL>(st, p.rank_kind);
-      const uint32_t taddr = lane_base + buf * kTileN;
-      const int64_t col_base = static_cast<int64_t>(tile_pos) * kTileN;
-      float ra[32], rb[32];
-      ptx::tmem_ld32(taddr, ra);
-      ptx::tmem_wait_ld();
-#pragma unroll 1
-      for (int c = 0; c < 8; c += 2) {
-        ptx::tmem_ld32(taddr + (c + 1) * 32, rb);
-        process_chunk<KL>(p, ra, scratch, col_base + c * 32, st);
-        __syncwarp();  // tcgen05.ld / wait::ld are warp-collective: reconverge after the slow path
+      const uint32_t taddr = lane_base + buf * kTileN + half * 128;
+      const int64_t col0 = static_cast<int64_t>(tile_pos) * kTileN + half * 128;
+      // Two chunks in flight at a time (one for 32-entry lists: register budget of 168 at 320
+      // threads); the other warp of this lane quarter overlaps its loads with this one's work.
+      float r0[32], r1[32];
+      if constexpr (KL >= 32) {
+        ptx::tmem_ld32(taddr, r0);
         ptx::tmem_wait_ld();
-        if (c + 2 < 8) {
-          ptx::tmem_ld32(taddr + (c + 2) * 32, ra);
-        } else {
-          // All 8 chunks of this accumulator are in registers: hand the buffer back.
-          ptx::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) ptx::mbar_arrive(&s.tempty[buf]);
-        }
-        process_chunk<KL>(p, rb, scratch, col_base + (c + 1) * 32, st);
-        __syncwarp();
-        if (c + 2 < 8) ptx::tmem_wait_ld();
+        process_chunk<KL>(p, r0, col0, st);
+        ptx::tmem_ld32(taddr + 32, r0);
+        ptx::tmem_wait_ld();
+        process_chunk<KL>(p, r0, col0 + 32, st);
+        ptx::tmem_ld32(taddr + 64, r0);
+        ptx::tmem_wait_ld();
+        process_chunk<KL>(p, r0, col0 + 64, st);
+        ptx::tmem_ld32(taddr + 96, r0);
+        ptx::tmem_wait_ld();
+      } else {
+        ptx::tmem_ld32(taddr, r0);
+        ptx::tmem_ld32(taddr + 32, r1);
+        ptx::tmem_wait_ld();
+        process_chunk<KL>(p, r0, col0, st);
+        process_chunk<KL>(p, r1, col0 + 32, st);
+        ptx::tmem_ld32(taddr + 64, r0);
+        ptx::tmem_ld32(taddr + 96, r1);
+        ptx::tmem_wait_ld();
+      }
+      // This warp's 128 columns are in registers: hand its share of the buffer back.
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&s.tempty[buf]);
+      if constexpr (KL >= 32) {
+        process_chunk<KL>(p, r0, col0 + 96, st);
+      } else {
+        process_chunk<KL>(p, r0, col0 + 64, st);
+        process_chunk<KL>(p, r1, col0 + 96, st);
       }
       ++tile;
     }
     if (!ok) return;
     if constexpr (KL > 0) {
       if (st.real) publish_bound<KL>(p, q, st);
-      uint64_t* dst = p.out + (static_cast<size_t>(q) * p.num_sc + it.sc) * KL;
+      uint64_t* dst =
+          p.out + ((static_cast<size_t>(q) * p.num_sc + it.sc) * kListsPerItem + half) * KL;
 #pragma unroll
       for (int i = 0; i < KL; ++i) dst[i] = st.L[i];
     }
@@ -456,7 +484,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       ptx::mbar_init(&s.tfull[i], 1);
-      ptx::mbar_init(&s.tempty[i], 4);
+      ptx::mbar_init(&s.tempty[i], kEpiWarps);
     }
     ptx::mbar_init(s.afull, 1);
     ptx::mbar_init(s.aempty, 1);
@@ -464,20 +492,20 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     *s.abort = 0;
     ptx::fence_barrier_init();
   }
-  if (warp == 4 && lane == 0) {
+  if (warp == kEpiWarps && lane == 0) {
     ptx::tma_prefetch_desc(&maps.a64);
     ptx::tma_prefetch_desc(&maps.b64);
   }
-  if (warp == 5) ptx::tmem_alloc(s.tmem_slot, kTmemCols);
+  if (warp == kEpiWarps + 1) ptx::tmem_alloc(s.tmem_slot, kTmemCols);
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *s.tmem_slot;
   const bool lo = p.query_split != 0 && *p.q_lo_flag != 0;
 
-  if (warp == 4) {
+  if (warp == kEpiWarps) {
     if (lane == 0) run_producer(p, maps, s, lo);
-  } else if (warp == 5) {
+  } else if (warp == kEpiWarps + 1) {
     if (lane == 0) run_mma(p, s, tmem_base, lo);
     __syncwarp();
   } else {
@@ -486,7 +514,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
 
   ptx::tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kEpiWarps + 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem_base, kTmemCols);
   }
@@ -515,18 +543,15 @@ bool plan_fused_smem(FusedParams& p, int max_smem_optin) {
     }
   }
   p.stage_off = off;
-  const int scratch_bytes = kTileQ * kScratchStride * 4;
   const int budget = max_smem_optin - 1024;  // alignment slack
   int stages = 8;
   for (; stages >= 2; --stages) {
     const int bar_bytes = (2 * stages + 7) * 8 + 16;
-    const int total = off + stages * kUnitBytes + scratch_bytes + bar_bytes;
-    if (total <= budget) break;
+    if (off + stages * kUnitBytes + bar_bytes <= budget) break;
   }
   if (stages < 2) return false;
   p.nstages = stages;
-  p.scratch_off = off + stages * kUnitBytes;
-  p.bar_off = p.scratch_off + scratch_bytes;
+  p.bar_off = off + stages * kUnitBytes;
   p.smem_bytes = p.bar_off + (2 * stages + 7) * 8 + 16 + 1024;
   return true;
 }

@@ -5,14 +5,16 @@
 // never exists. One CTA per SM loops over work items (query tile of 128, super-chunk of database
 // tiles of 256 rows):
 //
-//   warp 4  TMA producer   loads the query tile once per item (resident A) and streams database
+//   warp 8  TMA producer   loads the query tile once per item (resident A) and streams database
 //                          K-chunks (<= 64 fp16 columns x 256 rows) through an smem ring;
-//   warp 5  MMA issuer     tcgen05.mma kind::f16, M=128 (queries) x N=256 (rows), fp32
+//   warp 9  MMA issuer     tcgen05.mma kind::f16, M=128 (queries) x N=256 (rows), fp32
 //                          accumulators in TMEM, double-buffered (2 x 256 columns);
-//   warps 0-3 epilogue     each thread owns one query (one TMEM lane): tcgen05.ld 32 columns at
-//                          a time, a 3-input max tree against the query's current threshold,
-//                          and, rarely, an exact per-column check + insertion into a sorted
-//                          register list of the KL best (value, row id) keys.
+//   warps 0-7 epilogue     warps w and w+4 share TMEM lane quarter w (32 queries, one per
+//                          thread) and take 128 of the 256 columns each: four tcgen05.ld of 32
+//                          columns issued back to back, one wait, then per 32 columns a 3-input
+//                          max tree against the query's current threshold and, rarely, an exact
+//                          per-column check + insertion into the thread's sorted register list
+//                          of the KL best (value, row id) keys. Each half keeps its own list.
 //
 // Ranking values ("v", smaller is better) per query q and database position j, from the MMA dot
 // product s (queries and rows pre-scaled by powers of two, split into fp16 hi/lo parts when the
@@ -37,9 +39,10 @@ namespace prim {
 constexpr int kTileQ = 128;                // queries per tile: MMA M, TMEM lanes
 constexpr int kTileN = 256;                // database rows per tile: MMA N
 constexpr int kUnitBytes = kTileN * 128;   // one smem slot: a 64-column fp16 chunk of a tile
-constexpr int kFusedThreads = 192;         // warps 0-3 epilogue, 4 TMA, 5 MMA
+constexpr int kEpiWarps = 8;               // two warps per TMEM lane quarter, 128 columns each
+constexpr int kListsPerItem = 2;           // list-mode output: one sorted list per column half
+constexpr int kFusedThreads = 320;         // warps 0-7 epilogue, 8 TMA, 9 MMA
 constexpr int kMaxChunks = 8;              // padded dim <= 512 per part
-constexpr int kScratchStride = 33;         // floats per epilogue thread in the slow-path scratch
 constexpr int kTmemCols = 512;             // two 256-column fp32 accumulators
 
 enum RankKind : int { kRankAffine = 0, kRankScaled = 1, kRankColumnScaled = 2 };
@@ -67,7 +70,6 @@ struct FusedParams {
   int nunits;                      // smem units per database tile = b_parts * nchunk
   int nstages;                     // smem ring slots
   int stage_off;                   // smem byte offset of slot 0
-  int scratch_off;                 // smem byte offset of the slow-path scratch
   int bar_off;                     // smem byte offset of the mbarriers
   int smem_bytes;                  // dynamic smem requested (includes 1 KB alignment slack)
   int query_split;                 // 1: the query lo part is used when *q_lo_flag != 0
@@ -87,7 +89,8 @@ struct FusedParams {
   int64_t nq;                      // real queries (lanes >= nq are padding and never select)
   int k_pub;                       // rank (1-based) whose key a list publishes as a bound
   uint64_t* q_bound;               // [q_pad] smallest published k_pub-th key per query
-  uint64_t* out;                   // [q_pad][num_sc][KL] sorted keys (list mode)
+  uint64_t* out;                   // [q_pad][num_sc][2][KL] sorted keys (list mode; one list per
+                                   // column half)
   int* err;                        // watchdog word
   int tile_stride = 1;             // item tile ranges count every tile_stride-th database tile
   // Append mode (KL = 0): every column whose key is within the query's bound q_tau_key[q] is

@@ -17,7 +17,7 @@ namespace prim {
 
 struct MergeParams {
   const uint64_t* cand;      // [q_pad][num_sc][kl]
-  int num_sc;
+  int num_sc;                // sorted lists per query
   int kl;
   int64_t nq;
   int dim;
