@@ -21,6 +21,9 @@ struct Smem {
   uint64_t* afull;   // query tile landed
   uint64_t* aempty;  // MMA done with the query tile
   uint64_t* drain;   // final MMA completion
+  uint64_t* side_full;   // [kSideBufs] side data landed
+  uint64_t* side_empty;  // [kSideBufs] epilogue done with the slot (one arrival per warp)
+  uint8_t* side;         // [kSideBufs][kSideBytes]
   uint32_t* tmem_slot;
   volatile int* abort;
 };
@@ -36,7 +39,10 @@ __device__ __forceinline__ Smem carve(const FusedParams& p, uint8_t* raw) {
   s.afull = s.tempty + 2;
   s.aempty = s.afull + 1;
   s.drain = s.aempty + 1;
-  s.tmem_slot = reinterpret_cast<uint32_t*>(s.drain + 1);
+  s.side_full = s.drain + 1;
+  s.side_empty = s.side_full + kSideBufs;
+  s.side = s.base + p.side_off;
+  s.tmem_slot = reinterpret_cast<uint32_t*>(s.side_empty + kSideBufs);
   s.abort = reinterpret_cast<volatile int*>(s.tmem_slot + 1);
   return s;
 }
@@ -78,7 +84,9 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* 
 // TMA producer (one thread)
 // ------------------------------------------------------------------------------------------
 __device__ void run_producer(const FusedParams& p, const FusedMaps& maps, const Smem& s, bool lo) {
-  uint32_t unit = 0;
+  uint32_t unit = 0, tile = 0;
+  const bool need_aux = p.rank_kind != kRankScaled;
+  const uint32_t side_tx = (need_aux ? 1024u : 0u) + 1024u + (p.allow ? 32u : 0u);
   int a_loads = 0;
   int cur_qt = -1;
   bool ok = true;
@@ -102,6 +110,20 @@ __device__ void run_producer(const FusedParams& p, const FusedMaps& maps, const 
       cur_qt = it.qt;
     }
     for (int t = it.t0; t < it.t1 && ok; ++t) {
+      // Side data first: the epilogue needs it only after this tile's MMAs.
+      const uint32_t sb = tile % kSideBufs, suse = tile / kSideBufs;
+      if (suse > 0 && !ptx::mbar_wait(&s.side_empty[sb], (suse - 1) & 1, s.abort, p.err,
+                                      kErrWaitSideEmpty)) {
+        ok = false;
+        break;
+      }
+      const int64_t pos0 = static_cast<int64_t>(t) * p.tile_stride * kTileN;
+      uint8_t* slot_side = s.side + sb * kSideBytes;
+      ptx::mbar_arrive_expect_tx(&s.side_full[sb], side_tx);
+      if (need_aux) ptx::bulk_load(slot_side + kSideAuxOff, p.row_aux + pos0, 1024, &s.side_full[sb]);
+      ptx::bulk_load(slot_side + kSideIdOff, p.row_id + pos0, 1024, &s.side_full[sb]);
+      if (p.allow) ptx::bulk_load(slot_side + kSideAllowOff, p.allow + pos0 / 32, 32, &s.side_full[sb]);
+      ++tile;
       for (int u = 0; u < p.nunits; ++u) {
         const uint32_t slot = unit % p.nstages;
         const uint32_t use = unit / p.nstages;
@@ -127,15 +149,72 @@ __device__ void run_producer(const FusedParams& p, const FusedMaps& maps, const 
     drain_wait(&s.full[slot], (last / p.nstages) & 1, p.err);
   }
   if (a_loads > 0) drain_wait(s.afull, (a_loads - 1) & 1, p.err);
+  for (uint32_t sb = 0; sb < static_cast<uint32_t>(kSideBufs) && sb < tile; ++sb) {
+    const uint32_t last = ((tile - 1 - sb) / kSideBufs) * kSideBufs + sb;
+    drain_wait(&s.side_full[sb], (last / kSideBufs) & 1, p.err);
+  }
 }
 
 // ------------------------------------------------------------------------------------------
 // MMA issuer (one thread)
 // ------------------------------------------------------------------------------------------
-__device__ void run_mma(const FusedParams& p, const Smem& s, uint32_t tmem_base, bool lo) {
-  constexpr uint32_t kIdesc = ptx::idesc_f16_f32(kTileQ, kTileN);
+// One thread feeds the tensor core: at D=128 a tile is 8 MMAs of 128 cycles each, so the whole
+// per-tile loop (waits, fences, commits, descriptor arithmetic) has to stay under 1,024 cycles or
+// the tensor core idles. The loop therefore carries no branch between the MMAs of a unit: the
+// query-lo pass (LO) and the K steps per chunk (KS: 4, 2 or 1 for chunks of 64, 32 or 16
+// columns; 0 = chunks of mixed widths, dispatched once per chunk) are template parameters, and
+// run_mma_dispatch picks the instance once per launch. Descriptors are built once per chunk and
+// kept in registers (the chunk loop is unrolled over kMaxChunks so every index is static); the
+// ring position is tracked without division.
+constexpr uint32_t kIdesc = ptx::idesc_f16_f32(kTileQ, kTileN);
+// Descriptor address fields count 16-byte units; a K step of 16 fp16 values is 32 bytes.
+constexpr uint64_t kStepDesc = 32 >> 4;
+constexpr uint64_t kSlotDesc = kUnitBytes >> 4;
+
+// The MMAs of one unit (one chunk of one database part): K steps of 16, each against the query's
+// hi part and, with LO, its lo part. `acc` = 0 only for the first unit of a tile.
+template <bool LO, int KS>
+__device__ __forceinline__ void issue_unit(uint32_t d_tmem, uint64_t a_hi, uint64_t a_lo,
+                                           uint64_t bd, uint32_t acc) {
+  ptx::mma_f16_ss(d_tmem, a_hi, bd, kIdesc, acc);
+  if constexpr (LO) ptx::mma_f16_ss(d_tmem, a_lo, bd, kIdesc, 1);
+#pragma unroll
+  for (int ks = 1; ks < KS; ++ks) {
+    ptx::mma_f16_ss(d_tmem, a_hi + ks * kStepDesc, bd + ks * kStepDesc, kIdesc, 1);
+    if constexpr (LO) ptx::mma_f16_ss(d_tmem, a_lo + ks * kStepDesc, bd + ks * kStepDesc, kIdesc, 1);
+  }
+}
+
+template <bool LO, int KS>
+__device__ __forceinline__ void issue_chunk(uint32_t d_tmem, uint64_t a_hi, uint64_t a_lo,
+                                            uint64_t bd, uint32_t acc, int ksteps) {
+  if constexpr (KS > 0) {
+    issue_unit<LO, KS>(d_tmem, a_hi, a_lo, bd, acc);
+  } else if (ksteps == 4) {
+    issue_unit<LO, 4>(d_tmem, a_hi, a_lo, bd, acc);
+  } else if (ksteps == 2) {
+    issue_unit<LO, 2>(d_tmem, a_hi, a_lo, bd, acc);
+  } else {
+    issue_unit<LO, 1>(d_tmem, a_hi, a_lo, bd, acc);
+  }
+}
+
+template <bool LO, int KS>
+__device__ void run_mma(const FusedParams& p, const Smem& s, uint32_t tmem_base) {
   const uint32_t base_addr = ptx::smem_addr(s.base);
-  uint32_t unit = 0, tile = 0;
+  uint64_t a_hi[kMaxChunks], a_lo[kMaxChunks], b_base[kMaxChunks];
+  int ksteps[kMaxChunks];
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int w = c < p.nchunk ? p.chunk_w[c] : 16;
+    const uint32_t row_bytes = static_cast<uint32_t>(w * 2);
+    a_hi[c] = ptx::smem_desc(base_addr + p.a_off[0][c], row_bytes);
+    a_lo[c] = ptx::smem_desc(base_addr + p.a_off[1][c], row_bytes);
+    b_base[c] = ptx::smem_desc(base_addr + p.stage_off, row_bytes);
+    ksteps[c] = w / 16;
+  }
+  uint32_t slot = 0, phase = 0;
+  uint32_t tile = 0;
   int a_waits = 0, cur_qt = -1;
   bool ok = true;
   for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
@@ -159,29 +238,29 @@ __device__ void run_mma(const FusedParams& p, const Smem& s, uint32_t tmem_base,
       ptx::tc_fence_after();
       const uint32_t d_tmem = tmem_base + buf * kTileN;
       uint32_t acc = 0;
-      for (int u = 0; u < p.nunits; ++u) {
-        const uint32_t slot = unit % p.nstages;
-        const uint32_t suse = unit / p.nstages;
-        if (!ptx::mbar_wait(&s.full[slot], suse & 1, s.abort, p.err, kErrWaitSlotFull)) {
-          ok = false;
-          break;
-        }
-        ptx::tc_fence_after();
-        const int bp = u / p.nchunk, c = u % p.nchunk, w = p.chunk_w[c];
-        const uint32_t row_bytes = static_cast<uint32_t>(w * 2);
-        const uint32_t b_addr = base_addr + p.stage_off + slot * kUnitBytes;
-        const uint32_t a0 = base_addr + p.a_off[0][c];
-        const uint32_t a1 = base_addr + p.a_off[1][c];
-        for (int ks = 0; ks < w / 16; ++ks) {
-          const uint64_t bd = ptx::smem_desc(b_addr + ks * 32, row_bytes);
-          ptx::mma_f16_ss(d_tmem, ptx::smem_desc(a0 + ks * 32, row_bytes), bd, kIdesc, acc);
+      // Units arrive in the producer's order: database part bp major, chunk c minor. The query's
+      // lo part meets only the database hi part (bp == 0).
+      for (int bp = 0; bp < p.b_parts && ok; ++bp) {
+#pragma unroll
+        for (int c = 0; c < kMaxChunks; ++c) {
+          if (c >= p.nchunk) break;
+          if (!ptx::mbar_wait(&s.full[slot], phase, s.abort, p.err, kErrWaitSlotFull)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint64_t bd = b_base[c] + slot * kSlotDesc;
+          if (LO && bp == 0)
+            issue_chunk<true, KS>(d_tmem, a_hi[c], a_lo[c], bd, acc, ksteps[c]);
+          else
+            issue_chunk<false, KS>(d_tmem, a_hi[c], a_lo[c], bd, acc, ksteps[c]);
           acc = 1;
-          if (bp == 0 && lo) {
-            ptx::mma_f16_ss(d_tmem, ptx::smem_desc(a1 + ks * 32, row_bytes), bd, kIdesc, 1);
+          ptx::mma_commit(&s.empty[slot]);  // slot reusable once these MMAs have read it
+          if (++slot == static_cast<uint32_t>(p.nstages)) {
+            slot = 0;
+            phase ^= 1u;
           }
         }
-        ptx::mma_commit(&s.empty[slot]);  // slot reusable once these MMAs have read it
-        ++unit;
       }
       if (!ok) break;
       ptx::mma_commit(&s.tfull[buf]);
@@ -194,6 +273,24 @@ __device__ void run_mma(const FusedParams& p, const Smem& s, uint32_t tmem_base,
   // Unwind: wait until every MMA issued by this thread has completed before TMEM is released.
   ptx::mma_commit(s.drain);
   drain_wait(s.drain, 0, p.err);
+}
+
+// Picks the run_mma instance: LO from the launch's query-split flag, KS from the chunk widths
+// when they are all equal (0 = mixed).
+__device__ void run_mma_dispatch(const FusedParams& p, const Smem& s, uint32_t tmem_base, bool lo) {
+  int ks = p.chunk_w[0] / 16;
+  for (int c = 1; c < p.nchunk; ++c)
+    if (p.chunk_w[c] / 16 != ks) ks = 0;
+  if (lo) {
+    if (ks == 4) return run_mma<true, 4>(p, s, tmem_base);
+    if (ks == 2) return run_mma<true, 2>(p, s, tmem_base);
+    if (ks == 1) return run_mma<true, 1>(p, s, tmem_base);
+    return run_mma<true, 0>(p, s, tmem_base);
+  }
+  if (ks == 4) return run_mma<false, 4>(p, s, tmem_base);
+  if (ks == 2) return run_mma<false, 2>(p, s, tmem_base);
+  if (ks == 1) return run_mma<false, 1>(p, s, tmem_base);
+  return run_mma<false, 0>(p, s, tmem_base);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -217,15 +314,16 @@ __device__ __forceinline__ void list_insert(uint64_t (&L)[KL], uint64_t c) {
 //   column:  v = s*aux <= w with aux in [aux_min, aux_max] < 0  =>  s >= w / aux_min (w < 0)
 //                                                                   s >= w / aux_max (w >= 0)
 // The slack (1e-5 of the magnitudes involved) keeps the bound conservative against the rounding
-// of the exact per-column evaluation in the slow path.
-__device__ __forceinline__ float s_threshold(float w, float m, float2 ta, int kind) {
+// of the exact per-column evaluation in the slow path, and against the 1.5 ulp of dividing by m
+// through its reciprocal inv_m = 1/m (computed once per query).
+__device__ __forceinline__ float s_threshold(float w, float inv_m, float2 ta, int kind) {
   if (!(w < kInf)) return -kInf;
   float t, mag;
   if (kind == kRankAffine) {
-    t = (w - ta.x) / m;
-    mag = fabsf(t) + (fabsf(w) + fabsf(ta.x)) / fabsf(m);
+    t = (w - ta.x) * inv_m;
+    mag = fabsf(t) + (fabsf(w) + fabsf(ta.x)) * fabsf(inv_m);
   } else if (kind == kRankScaled) {
-    t = w / m;
+    t = w * inv_m;
     mag = fabsf(t);
   } else {
     t = (w < 0.f) ? w / ta.x : w / ta.y;
@@ -257,6 +355,7 @@ template <int KL>
 struct EpiState {
   uint64_t L[KL > 0 ? KL : 1];
   float m;
+  float inv_m;    // 1 / m
   float thr;      // s-space threshold for the current tile
   float gw;       // ranking value of the shared per-query bound (+ slack), NaN when none
   float2 ta;
@@ -277,10 +376,10 @@ __device__ __forceinline__ void refresh_threshold(EpiState<KL>& st, int kind) {
     return;
   }
   if constexpr (KL == 0) {  // append mode: fixed per-query threshold (already has its slack)
-    st.thr = s_threshold(st.gw, st.m, st.ta, kind);
+    st.thr = s_threshold(st.gw, st.inv_m, st.ta, kind);
   } else {
     const float own = keys::key_value(st.L[KL - 1]);  // NaN while the list is not full
-    st.thr = s_threshold(fminf(own, st.gw), st.m, st.ta, kind);
+    st.thr = s_threshold(fminf(own, st.gw), st.inv_m, st.ta, kind);
   }
 }
 
@@ -327,7 +426,13 @@ __device__ __forceinline__ float pick32(const float (&r)[32], int j) {
 
 template <int KL>
 __device__ __forceinline__ void slow_path(const FusedParams& p, const float (&r)[32],
-                                          int64_t col0, EpiState<KL>& st) {
+                                          int64_t col0, int ct0, const uint8_t* side,
+                                          EpiState<KL>& st) {
+  // Per-column data of this tile, staged in shared memory by the producer (column ct of the
+  // tile: aux[ct], id[ct], allow bit ct).
+  const float* aux = reinterpret_cast<const float*>(side + kSideAuxOff);
+  const uint32_t* ids = reinterpret_cast<const uint32_t*>(side + kSideIdOff);
+  const uint32_t* allow = reinterpret_cast<const uint32_t*>(side + kSideAllowOff);
   // Visit only the columns that pass the conservative bound (NaN passes: its exact key is
   // decided below).
   uint32_t mask = 0;
@@ -341,17 +446,18 @@ __device__ __forceinline__ void slow_path(const FusedParams& p, const float (&r)
     const int64_t pos = col0 + j;
     if (pos >= p.n_rows) break;
     float v;
-    const bool allowed = p.allow == nullptr || ((p.allow[pos >> 5] >> (pos & 31)) & 1u);
+    const int ct = ct0 + j;
+    const bool allowed = p.allow == nullptr || ((allow[ct >> 5] >> (ct & 31)) & 1u);
     if (!allowed) {
       v = kInf;
     } else if (p.rank_kind == kRankAffine) {
-      v = fmaf(sv, st.m, p.row_aux[pos]);
+      v = fmaf(sv, st.m, aux[ct]);
     } else if (p.rank_kind == kRankScaled) {
       v = sv * st.m;
     } else {
-      v = sv * p.row_aux[pos];
+      v = sv * aux[ct];
     }
-    const uint64_t key = keys::make_key(v, p.row_id[pos]);
+    const uint64_t key = keys::make_key(v, ids[ct]);
     if constexpr (KL == 0) {
       if (st.by_key ? key <= st.gkey : v <= st.gw) {
         const uint32_t slot = atomicAdd(p.app_count + st.qi, 1u);
@@ -369,9 +475,10 @@ __device__ __forceinline__ void slow_path(const FusedParams& p, const float (&r)
 
 template <int KL>
 __device__ __forceinline__ void process_chunk(const FusedParams& p, const float (&r)[32],
-                                              int64_t col0, EpiState<KL>& st) {
+                                              int64_t col0, int ct0, const uint8_t* side,
+                                              EpiState<KL>& st) {
   const float g = max32(r);
-  if (!(g < st.thr)) slow_path<KL>(p, r, col0, st);
+  if (!(g < st.thr)) slow_path<KL>(p, r, col0, ct0, side, st);
   __syncwarp();  // tcgen05.ld / wait::ld are warp-collective: reconverge after the slow path
 }
 
@@ -386,9 +493,11 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
     const Item it = item_of(p, item);
     const int64_t q = static_cast<int64_t>(it.qt) * kTileQ + quarter * 32 + lane;
     st.m = p.q_mul[q];
+    st.inv_m = 1.0f / st.m;
     st.real = q < p.nq;
     st.qi = q;
-    st.ta = p.tile_aux[it.t0 * p.tile_stride];
+    // Aux ranges are loaded one tile ahead.
+    float2 ta_next = p.tile_aux[it.t0 * p.tile_stride];
     if constexpr (KL > 0) {
       read_bound<KL>(p, q, st);
 #pragma unroll
@@ -396,19 +505,14 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
     } else {
       st.gkey = p.q_tau_key[q];
     }
-    bool ok = true;
-    for (int t = it.t0; t < it.t1; ++t) {
-      const uint32_t buf = tile & 1, use = tile >> 1;
-      // Warp-uniform decision: tcgen05.ld below is warp-collective, so either every lane
-      // proceeds or every lane unwinds.
-      const bool got = ptx::mbar_wait(&s.tfull[buf], use & 1, s.abort, p.err, kErrWaitTmemFull);
-      if (!__all_sync(0xffffffffu, got)) {
-        ok = false;
-        break;
-      }
-      ptx::tc_fence_after();
+    // Everything tile t's filter needs (aux range, shared bound, threshold) is known once tile
+    // t-1 is done, so it is prepared then, while the next TMEM buffer is still being filled:
+    // after the buffer fills, this warp goes straight to reading it and hands it back sooner,
+    // which is what lets the MMA of tile t+2 start before the tensor core runs dry.
+    auto prepare = [&](int t) {
       const int tile_pos = t * p.tile_stride;
-      st.ta = p.tile_aux[tile_pos];
+      st.ta = ta_next;
+      if (t + 1 < it.t1) ta_next = p.tile_aux[tile_pos + p.tile_stride];
       if constexpr (KL > 0) {
         if (((t - it.t0) & (kBoundPeriod - 1)) == kBoundPeriod - 1 && st.real) {
           publish_bound<KL>(p, q, st);
@@ -420,6 +524,24 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
         st.gw = st.by_key ? tv : append_limit(tv, st.ta);
       }
       refresh_threshold<KL>(st, p.rank_kind);
+    };
+    prepare(it.t0);
+    bool ok = true;
+    for (int t = it.t0; t < it.t1; ++t) {
+      const uint32_t buf = tile & 1, use = tile >> 1;
+      // Warp-uniform decision: tcgen05.ld below is warp-collective, so either every lane
+      // proceeds or every lane unwinds.
+      const uint32_t sb = tile % kSideBufs, suse = tile / kSideBufs;
+      bool got = ptx::mbar_wait(&s.tfull[buf], use & 1, s.abort, p.err, kErrWaitTmemFull);
+      got = got && ptx::mbar_wait(&s.side_full[sb], suse & 1, s.abort, p.err, kErrWaitSideFull);
+      if (!__all_sync(0xffffffffu, got)) {
+        ok = false;
+        break;
+      }
+      ptx::tc_fence_after();
+      const uint8_t* side = s.side + sb * kSideBytes;
+      const int ct0 = half * 128;  // this warp's first column within the tile
+      const int tile_pos = t * p.tile_stride;
       const uint32_t taddr = lane_base + buf * kTileN + half * 128;
       const int64_t col0 = static_cast<int64_t>(tile_pos) * kTileN + half * 128;
       // Two chunks in flight at a time (one for 32-entry lists: register budget of 168 at 320
@@ -428,21 +550,21 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
       if constexpr (KL >= 32) {
         ptx::tmem_ld32(taddr, r0);
         ptx::tmem_wait_ld();
-        process_chunk<KL>(p, r0, col0, st);
+        process_chunk<KL>(p, r0, col0, ct0, side, st);
         ptx::tmem_ld32(taddr + 32, r0);
         ptx::tmem_wait_ld();
-        process_chunk<KL>(p, r0, col0 + 32, st);
+        process_chunk<KL>(p, r0, col0 + 32, ct0 + 32, side, st);
         ptx::tmem_ld32(taddr + 64, r0);
         ptx::tmem_wait_ld();
-        process_chunk<KL>(p, r0, col0 + 64, st);
+        process_chunk<KL>(p, r0, col0 + 64, ct0 + 64, side, st);
         ptx::tmem_ld32(taddr + 96, r0);
         ptx::tmem_wait_ld();
       } else {
         ptx::tmem_ld32(taddr, r0);
         ptx::tmem_ld32(taddr + 32, r1);
         ptx::tmem_wait_ld();
-        process_chunk<KL>(p, r0, col0, st);
-        process_chunk<KL>(p, r1, col0 + 32, st);
+        process_chunk<KL>(p, r0, col0, ct0, side, st);
+        process_chunk<KL>(p, r1, col0 + 32, ct0 + 32, side, st);
         ptx::tmem_ld32(taddr + 64, r0);
         ptx::tmem_ld32(taddr + 96, r1);
         ptx::tmem_wait_ld();
@@ -452,12 +574,16 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&s.tempty[buf]);
       if constexpr (KL >= 32) {
-        process_chunk<KL>(p, r0, col0 + 96, st);
+        process_chunk<KL>(p, r0, col0 + 96, ct0 + 96, side, st);
       } else {
-        process_chunk<KL>(p, r0, col0 + 64, st);
-        process_chunk<KL>(p, r1, col0 + 96, st);
+        process_chunk<KL>(p, r0, col0 + 64, ct0 + 64, side, st);
+        process_chunk<KL>(p, r1, col0 + 96, ct0 + 96, side, st);
       }
+      // Side slot released once this warp's exact checks of the tile are done.
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&s.side_empty[sb]);
       ++tile;
+      if (t + 1 < it.t1) prepare(t + 1);
     }
     if (!ok) return;
     if constexpr (KL > 0) {
@@ -489,6 +615,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     ptx::mbar_init(s.afull, 1);
     ptx::mbar_init(s.aempty, 1);
     ptx::mbar_init(s.drain, 1);
+    for (int i = 0; i < kSideBufs; ++i) {
+      ptx::mbar_init(&s.side_full[i], 1);
+      ptx::mbar_init(&s.side_empty[i], kEpiWarps);
+    }
     *s.abort = 0;
     ptx::fence_barrier_init();
   }
@@ -506,7 +636,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   if (warp == kEpiWarps) {
     if (lane == 0) run_producer(p, maps, s, lo);
   } else if (warp == kEpiWarps + 1) {
-    if (lane == 0) run_mma(p, s, tmem_base, lo);
+    if (lane == 0) run_mma_dispatch(p, s, tmem_base, lo);
     __syncwarp();
   } else {
     run_epilogue<KL>(p, s, tmem_base);
@@ -542,17 +672,19 @@ bool plan_fused_smem(FusedParams& p, int max_smem_optin) {
       p.a_tx_bytes[part] += bytes;
     }
   }
+  p.side_off = off;
+  off += (kSideBufs * kSideBytes + 1023) & ~1023;  // stages stay 1024-aligned (128B swizzle)
   p.stage_off = off;
   const int budget = max_smem_optin - 1024;  // alignment slack
+  auto bar_bytes = [](int stages) { return (2 * stages + 7 + 2 * kSideBufs) * 8 + 16; };
   int stages = 8;
   for (; stages >= 2; --stages) {
-    const int bar_bytes = (2 * stages + 7) * 8 + 16;
-    if (off + stages * kUnitBytes + bar_bytes <= budget) break;
+    if (off + stages * kUnitBytes + bar_bytes(stages) <= budget) break;
   }
   if (stages < 2) return false;
   p.nstages = stages;
   p.bar_off = off + stages * kUnitBytes;
-  p.smem_bytes = p.bar_off + (2 * stages + 7) * 8 + 16 + 1024;
+  p.smem_bytes = p.bar_off + bar_bytes(stages) + 1024;
   return true;
 }
 

@@ -6,7 +6,9 @@
 // tiles of 256 rows):
 //
 //   warp 8  TMA producer   loads the query tile once per item (resident A) and streams database
-//                          K-chunks (<= 64 fp16 columns x 256 rows) through an smem ring;
+//                          K-chunks (<= 64 fp16 columns x 256 rows) through an smem ring, plus
+//                          per tile the rows' aux values, ids and allow bits (2 KB) into a
+//                          4-deep side ring that the epilogue reads on its exact path;
 //   warp 9  MMA issuer     tcgen05.mma kind::f16, M=128 (queries) x N=256 (rows), fp32
 //                          accumulators in TMEM, double-buffered (2 x 256 columns);
 //   warps 0-7 epilogue     warps w and w+4 share TMEM lane quarter w (32 queries, one per
@@ -44,6 +46,11 @@ constexpr int kListsPerItem = 2;           // list-mode output: one sorted list 
 constexpr int kFusedThreads = 320;         // warps 0-7 epilogue, 8 TMA, 9 MMA
 constexpr int kMaxChunks = 8;              // padded dim <= 512 per part
 constexpr int kTmemCols = 512;             // two 256-column fp32 accumulators
+constexpr int kSideBufs = 4;               // side ring depth (tiles)
+constexpr int kSideAuxOff = 0;             // side slot: aux[256] fp32
+constexpr int kSideIdOff = 1024;           //            row id[256] u32
+constexpr int kSideAllowOff = 2048;        //            allow bits[256] (8 words)
+constexpr int kSideBytes = 2176;           // slot stride (multiple of 128 bytes)
 
 enum RankKind : int { kRankAffine = 0, kRankScaled = 1, kRankColumnScaled = 2 };
 
@@ -57,6 +64,8 @@ enum WatchdogCode : int {
   kErrWaitTmemFull = 0x105,
   kErrWaitAEmpty = 0x106,
   kErrDrain = 0x107,
+  kErrWaitSideEmpty = 0x108,
+  kErrWaitSideFull = 0x109,
 };
 
 struct FusedParams {
@@ -70,6 +79,7 @@ struct FusedParams {
   int nunits;                      // smem units per database tile = b_parts * nchunk
   int nstages;                     // smem ring slots
   int stage_off;                   // smem byte offset of slot 0
+  int side_off;                    // smem byte offset of the side ring
   int bar_off;                     // smem byte offset of the mbarriers
   int smem_bytes;                  // dynamic smem requested (includes 1 KB alignment slack)
   int query_split;                 // 1: the query lo part is used when *q_lo_flag != 0
