@@ -58,8 +58,9 @@ int list_size_for(int64_t k_eff) {
   return 0;
 }
 
-// Number of super-chunks per query tile: balances the per-CTA work of the statically strided
-// item schedule (every CTA runs items b, b + grid, ...) against the per-item overhead.
+// Number of super-chunks per query pair-tile: balances the per-pair work of the statically
+// strided item schedule (CTA pair c runs items c, c + pairs, ...) against the per-item
+// overhead.
 int choose_num_sc(int num_qtiles, int num_dbtiles, int num_sms, int64_t cand_per_sc_bytes,
                   int* tiles_per_item) {
   int best_sc = 1, best_L = num_dbtiles;
@@ -70,8 +71,8 @@ int choose_num_sc(int num_qtiles, int num_dbtiles, int num_sms, int64_t cand_per
     const int sc_eff = (num_dbtiles + L - 1) / L;
     if (sc_eff != sc) continue;
     if (static_cast<double>(cand_per_sc_bytes) * sc > 1.5e9) break;
-    const int64_t items = static_cast<int64_t>(num_qtiles) * sc;
-    const int64_t grid = std::min<int64_t>(items, num_sms);
+    const int64_t items = static_cast<int64_t>(num_qtiles / 2) * sc;
+    const int64_t grid = std::min<int64_t>(items, num_sms / 2);
     const int64_t waves = (items + grid - 1) / grid;
     const double cost = static_cast<double>(waves) * (L + kItemOverheadTiles);
     if (cost < best * 0.999) {
@@ -155,7 +156,7 @@ ovvsStatus build_from_device(rt::Resources& r, BruteIndex& ix, const void* d_dat
   OVVS_TRY_CUDA(ix.norm_sorted.reserve(ix.n_pad * sizeof(float)));
   OVVS_TRY_CUDA(ix.row_id.reserve(ix.n_pad * sizeof(uint32_t)));
   OVVS_TRY_CUDA(ix.inv_perm.reserve(n * sizeof(uint32_t)));
-  OVVS_TRY_CUDA(ix.tile_aux.reserve(ix.num_tiles * sizeof(float2)));
+  OVVS_TRY_CUDA(ix.tile_aux.reserve((ix.num_tiles + prim::group_count(ix.num_tiles)) * sizeof(float2)));
   prim::launch_scatter_rows(d_data, dtype, n, ix.n_pad, static_cast<int>(dim), ix.dp, ix.b_parts,
                             ix.metric, ix.e_db, perm.as<uint32_t>(), norm.as<float>(),
                             key.as<float>(), ix.rows16.as<__half>(),
@@ -168,9 +169,9 @@ ovvsStatus build_from_device(rt::Resources& r, BruteIndex& ix, const void* d_dat
   if (!keep_exact32) ix.exact32.release();
 
   const uint64_t cols = static_cast<uint64_t>(stride);
-  if (!rt::encode_f16_2d(&ix.b64, ix.rows16.get(), cols, ix.n_pad, 64, kTileN) ||
-      !rt::encode_f16_2d(&ix.b32, ix.rows16.get(), cols, ix.n_pad, 32, kTileN) ||
-      !rt::encode_f16_2d(&ix.b16, ix.rows16.get(), cols, ix.n_pad, 16, kTileN)) {
+  if (!rt::encode_f16_2d(&ix.b64, ix.rows16.get(), cols, ix.n_pad, 64, prim::kHalfN) ||
+      !rt::encode_f16_2d(&ix.b32, ix.rows16.get(), cols, ix.n_pad, 32, prim::kHalfN) ||
+      !rt::encode_f16_2d(&ix.b16, ix.rows16.get(), cols, ix.n_pad, 16, prim::kHalfN)) {
     return OVVS_STATUS_ERROR;
   }
   OVVS_TRY_CUDA(cudaStreamSynchronize(s));
@@ -229,7 +230,7 @@ ovvsStatus base_params(rt::Resources& r, const BruteIndex& ix, const SearchCtx& 
   p.num_dbtiles = ix.num_tiles;
   p.n_rows = ix.n;
   p.row_aux = ix.aux.as<float>();
-  p.tile_aux = ix.tile_aux.as<float2>();
+  p.group_aux = ix.tile_aux.as<float2>() + ix.num_tiles;
   p.row_id = ix.row_id.as<uint32_t>();
   p.q_mul = c.q_mul;
   p.allow = c.allow;
@@ -259,8 +260,13 @@ prim::MergeParams merge_params(const BruteIndex& ix, const SearchCtx& c, const f
   return m;
 }
 
+// SMs the fused kernel can use at once: two per co-resident CTA pair.
+int pair_sms(const rt::Resources& r, const prim::FusedParams& p) {
+  return 2 * std::min(r.num_sms / 2, prim::fused_max_pairs(p.smem_bytes));
+}
+
 int launch_grid(const prim::FusedParams& p, int num_sms) {
-  return static_cast<int>(std::min<int64_t>(p.num_items, num_sms));
+  return prim::fused_grid(p.num_items, num_sms);
 }
 
 // Large k (k plus re-rank margin above the register lists): bound pre-pass on a sample of the
@@ -298,7 +304,7 @@ ovvsStatus search_large(rt::Resources& r, const BruteIndex& ix, const SearchCtx&
     p.num_dbtiles = sampled;
     const int64_t cand_per_sc =
         c.q_pad * 32 * prim::kListsPerItem * static_cast<int64_t>(sizeof(uint64_t));
-    int num_sc = choose_num_sc(c.num_qtiles, sampled, r.num_sms, cand_per_sc, &p.tiles_per_item);
+    int num_sc = choose_num_sc(c.num_qtiles, sampled, pair_sms(r, p), cand_per_sc, &p.tiles_per_item);
     const int min_sc = static_cast<int>(
         std::min<int64_t>(sampled, (2 * need + 32 * prim::kListsPerItem - 1) /
                                        (32 * prim::kListsPerItem)));
@@ -309,7 +315,7 @@ ovvsStatus search_large(rt::Resources& r, const BruteIndex& ix, const SearchCtx&
     const int lists = num_sc * prim::kListsPerItem;
     if (lists <= 256 && static_cast<int64_t>(lists) * 32 >= need) {
       p.num_sc = num_sc;
-      p.num_items = c.num_qtiles * num_sc;
+      p.num_items = prim::fused_items(c.num_qtiles, num_sc);
       p.k_pub = 0;  // lists of 32 cannot bound rank `need`
       uint64_t* cand = nullptr;
       uint64_t* shared_bound = nullptr;
@@ -318,15 +324,15 @@ ovvsStatus search_large(rt::Resources& r, const BruteIndex& ix, const SearchCtx&
       OVVS_TRY_CUDA(cudaMemsetAsync(shared_bound, 0xFF, static_cast<size_t>(c.q_pad) * 8, s));
       p.q_bound = shared_bound;
       p.out = cand;
-      OVVS_TRY_CUDA(prim::launch_knn_fused(c.maps, p, 32, launch_grid(p, r.num_sms), s));
+      OVVS_TRY_CUDA(prim::launch_knn_fused(c.maps, p, 32, launch_grid(p, pair_sms(r, p)), s));
       OVVS_TRY_CUDA(prim::launch_kth_bound(cand, lists, nq, static_cast<int>(need), tau, s));
     }
   }
 
   prim::FusedParams p;
   OVVS_TRY(base_params(r, ix, c, nq, &p));
-  p.num_sc = choose_num_sc(c.num_qtiles, ix.num_tiles, r.num_sms, 0, &p.tiles_per_item);
-  p.num_items = c.num_qtiles * p.num_sc;
+  p.num_sc = choose_num_sc(c.num_qtiles, ix.num_tiles, pair_sms(r, p), 0, &p.tiles_per_item);
+  p.num_items = prim::fused_items(c.num_qtiles, p.num_sc);
   p.q_tau_key = tau;
   p.app_count = count;
   p.app_buf = buf;
@@ -344,7 +350,7 @@ ovvsStatus search_large(rt::Resources& r, const BruteIndex& ix, const SearchCtx&
     p.app_exact = round >= 2;  // persistent overflow: strict key bound (ties cannot pile up)
     OVVS_TRY_CUDA(cudaMemsetAsync(count, 0, static_cast<size_t>(c.q_pad) * sizeof(uint32_t), s));
     OVVS_TRY_CUDA(cudaMemsetAsync(overflow, 0, sizeof(int), s));
-    OVVS_TRY_CUDA(prim::launch_knn_fused(c.maps, p, 0, launch_grid(p, r.num_sms), s));
+    OVVS_TRY_CUDA(prim::launch_knn_fused(c.maps, p, 0, launch_grid(p, pair_sms(r, p)), s));
     OVVS_TRY_CUDA(prim::launch_select_rerank(sp, s));
     int host_overflow = 0;
     OVVS_TRY_CUDA(cudaMemcpyAsync(&host_overflow, overflow, sizeof(int), cudaMemcpyDeviceToHost, s));
@@ -367,7 +373,7 @@ ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_
   const int dim = static_cast<int>(ix.dim);
 
   SearchCtx c;
-  c.q_pad = (nq + kTileQ - 1) / kTileQ * kTileQ;
+  c.q_pad = prim::pad_queries(nq);
   c.num_qtiles = static_cast<int>(c.q_pad / kTileQ);
   r.mark(0);
   OVVS_TRY(r.scratch(rt::kWsQueryA, static_cast<size_t>(c.q_pad) * 2 * ix.dp, &c.a16));
@@ -420,9 +426,9 @@ ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_
     OVVS_TRY(base_params(r, ix, c, nq, &p));
     const int64_t cand_per_sc =
         c.q_pad * kl * prim::kListsPerItem * static_cast<int64_t>(sizeof(uint64_t));
-    p.num_sc = choose_num_sc(c.num_qtiles, ix.num_tiles, r.num_sms, cand_per_sc,
+    p.num_sc = choose_num_sc(c.num_qtiles, ix.num_tiles, pair_sms(r, p), cand_per_sc,
                              &p.tiles_per_item);
-    p.num_items = c.num_qtiles * p.num_sc;
+    p.num_items = prim::fused_items(c.num_qtiles, p.num_sc);
     uint64_t* cand = nullptr;
     OVVS_TRY(r.scratch(rt::kWsCand,
                        static_cast<size_t>(c.q_pad) * p.num_sc * prim::kListsPerItem * kl, &cand));
@@ -433,7 +439,7 @@ ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_
     p.q_bound = bound;
     p.k_pub = static_cast<int>(k_eff);
     r.mark(1);
-    OVVS_TRY_CUDA(prim::launch_knn_fused(c.maps, p, kl, launch_grid(p, r.num_sms), s));
+    OVVS_TRY_CUDA(prim::launch_knn_fused(c.maps, p, kl, launch_grid(p, pair_sms(r, p)), s));
     r.mark(2);
     m.cand = cand;
     m.num_sc = p.num_sc * prim::kListsPerItem;  // lists per query

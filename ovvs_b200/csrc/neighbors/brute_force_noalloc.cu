@@ -103,7 +103,7 @@ extern "C" ovvsStatus ovvsBruteForceSearchDeviceNoAlloc(ovvsResources_t res,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 
   // Size the pieces and reject what does not fit the fixed array.
-  const int64_t q_pad = (nq + prim::kTileQ - 1) / prim::kTileQ * prim::kTileQ;
+  const int64_t q_pad = prim::pad_queries(nq);
   const int num_qtiles = static_cast<int>(q_pad / prim::kTileQ);
   const size_t fixed = piece(sizeof(int)) + piece(sizeof(int)) +
                        piece(static_cast<size_t>(q_pad) * 2 * ix.dp * sizeof(__half)) +
@@ -127,7 +127,8 @@ extern "C" ovvsStatus ovvsBruteForceSearchDeviceNoAlloc(ovvsResources_t res,
   // The planner caps the candidate lists at 1.5e9 bytes; scale the per-super-chunk size so that
   // its cap lands on this array's budget instead.
   const double scale = 1.5e9 / static_cast<double>(cand_budget);
-  p.num_sc = nb::choose_num_sc(num_qtiles, ix.num_tiles, r.num_sms,
+  const int sms = 2 * std::min(r.num_sms / 2, prim::fused_max_pairs(p.smem_bytes));
+  p.num_sc = nb::choose_num_sc(num_qtiles, ix.num_tiles, sms,
                                static_cast<int64_t>(static_cast<double>(cand_per_sc) * scale) + 1,
                                &p.tiles_per_item);
   if (static_cast<size_t>(p.num_sc) * cand_per_sc > cand_budget) return OVVS_STATUS_SHAPE_MISMATCH;
@@ -161,10 +162,10 @@ extern "C" ovvsStatus ovvsBruteForceSearchDeviceNoAlloc(ovvsResources_t res,
   p.q_lo_flag = flag;
   p.num_qtiles = num_qtiles;
   p.num_dbtiles = ix.num_tiles;
-  p.num_items = num_qtiles * p.num_sc;
+  p.num_items = prim::fused_items(num_qtiles, p.num_sc);
   p.n_rows = ix.n;
   p.row_aux = ix.aux.as<float>();
-  p.tile_aux = ix.tile_aux.as<float2>();
+  p.group_aux = ix.tile_aux.as<float2>() + ix.num_tiles;
   p.row_id = ix.row_id.as<uint32_t>();
   p.q_mul = q_mul;
   p.allow = allow;
@@ -183,7 +184,7 @@ extern "C" ovvsStatus ovvsBruteForceSearchDeviceNoAlloc(ovvsResources_t res,
   maps.b64 = ix.b64;
   maps.b32 = ix.b32;
   maps.b16 = ix.b16;
-  const int grid = static_cast<int>(std::min<int64_t>(p.num_items, r.num_sms));
+  const int grid = prim::fused_grid(p.num_items, sms);
   OVVS_TRY_CUDA(prim::launch_knn_fused(maps, p, kl, grid, s));
 
   prim::MergeParams m{};

@@ -1,8 +1,13 @@
 // Fused distance + top-k kernel. Design notes in knn_fused.cuh.
 #include "knn_fused.cuh"
+#include "prep.cuh"
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+
+#include <map>
+#include <mutex>
+#include <utility>
 
 namespace ovvs {
 namespace prim {
@@ -24,6 +29,7 @@ struct Smem {
   uint64_t* side_full;   // [kSideBufs] side data landed
   uint64_t* side_empty;  // [kSideBufs] epilogue done with the slot (one arrival per warp)
   uint8_t* side;         // [kSideBufs][kSideBytes]
+  float* defer;          // [kEpiWarps * 32][kDeferStride] one deferred chunk row per epilogue lane
   uint32_t* tmem_slot;
   volatile int* abort;
 };
@@ -42,6 +48,7 @@ __device__ __forceinline__ Smem carve(const FusedParams& p, uint8_t* raw) {
   s.side_full = s.drain + 1;
   s.side_empty = s.side_full + kSideBufs;
   s.side = s.base + p.side_off;
+  s.defer = reinterpret_cast<float*>(s.base + p.defer_off);
   s.tmem_slot = reinterpret_cast<uint32_t*>(s.side_empty + kSideBufs);
   s.abort = reinterpret_cast<volatile int*>(s.tmem_slot + 1);
   return s;
@@ -53,27 +60,37 @@ __device__ __forceinline__ const CUtensorMap* pick_map(int w, const CUtensorMap*
   return w == 64 ? m64 : (w == 32 ? m32 : m16);
 }
 
-// Work item -> (query tile, super-chunk, tile range). Items are ordered super-chunk-major so
-// that CTAs running at the same time stream the same database tiles (L2 reuse).
+// Work item -> (query pair-tile, super-chunk, tile range); this CTA's query tile is
+// qt = 2 * pair-tile + rank. Items are ordered super-chunk-major so that pairs running at the
+// same time stream the same database tiles (L2 reuse). Pair c of the grid runs items c, c +
+// pairs, c + 2 * pairs, ...
 struct Item {
   int qt, sc, t0, t1;
 };
-__device__ __forceinline__ Item item_of(const FusedParams& p, int item) {
+__device__ __forceinline__ Item item_of(const FusedParams& p, int item, uint32_t rank) {
+  const int num_qpairs = p.num_qtiles >> 1;
   Item it;
-  it.qt = item % p.num_qtiles;
-  it.sc = item / p.num_qtiles;
+  const int qp = item % num_qpairs;
+  it.qt = 2 * qp + static_cast<int>(rank);
+  it.sc = item / num_qpairs;
   it.t0 = it.sc * p.tiles_per_item;
   it.t1 = min(it.t0 + p.tiles_per_item, p.num_dbtiles);
   return it;
 }
+__device__ __forceinline__ int first_item() { return static_cast<int>(blockIdx.x >> 1); }
+__device__ __forceinline__ int item_step() { return static_cast<int>(gridDim.x >> 1); }
 
 // Bounded wait used only while unwinding: ignores the abort flag (the copies or MMAs it waits
-// for complete on their own), still gives up after the time limit.
-__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* err) {
+// for complete on their own), still gives up after the time limit: the normal limit when the
+// CTA finished its work, 20 ms after an abort (in-flight copies land within microseconds; the
+// phase may never complete because the other role stopped).
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* err,
+                                           volatile int* abort) {
   if (ptx::mbar_try_wait(bar, parity)) return;
+  const uint64_t limit = *abort ? 20000000ull : ptx::kWaitLimitNs;
   const uint64_t t0 = ptx::globaltimer();
   while (!ptx::mbar_try_wait(bar, parity)) {
-    if (ptx::globaltimer() - t0 > ptx::kWaitLimitNs) {
+    if (ptx::globaltimer() - t0 > limit) {
       atomicCAS(err, 0, kErrDrain);
       return;
     }
@@ -83,27 +100,40 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* 
 // ------------------------------------------------------------------------------------------
 // TMA producer (one thread)
 // ------------------------------------------------------------------------------------------
-__device__ void run_producer(const FusedParams& p, const FusedMaps& maps, const Smem& s, bool lo) {
+// Both CTAs of the pair run a producer: each loads its own 128 queries and its own 128-row half
+// of every database chunk into its own shared memory. The copies are counted on the leader's
+// full / afull barriers (the leader arms them with the bytes of both CTAs); each producer learns
+// that a slot may be refilled from its own empty / aempty barrier, which the leader's MMA
+// commits reach in both CTAs.
+__device__ void run_producer(const FusedParams& p, const FusedMaps& maps, const Smem& s, bool lo,
+                             uint32_t rank) {
+  const bool leader = rank == 0;
+  const uint32_t full_l = ptx::peer_addr(s.full, 0);  // leader's full[0]
+  const uint32_t afull_l = ptx::peer_addr(s.afull, 0);
   uint32_t unit = 0, tile = 0;
+  uint32_t slot = 0, phase = 0;  // ring position; `phase` = parity of the current pass
+  bool wrapped = false;          // a slot is refilled only after its previous use was consumed
   const bool need_aux = p.rank_kind != kRankScaled;
   const uint32_t side_tx = (need_aux ? 1024u : 0u) + 1024u + (p.allow ? 32u : 0u);
   int a_loads = 0;
   int cur_qt = -1;
   bool ok = true;
-  for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
-    const Item it = item_of(p, item);
+  for (int item = first_item(); item < p.num_items && ok; item += item_step()) {
+    const Item it = item_of(p, item, rank);
     if (it.qt != cur_qt) {
       if (a_loads > 0 &&
           !ptx::mbar_wait(s.aempty, (a_loads - 1) & 1, s.abort, p.err, kErrWaitAEmpty)) {
         ok = false;
         break;
       }
-      ptx::mbar_arrive_expect_tx(s.afull, p.a_tx_bytes[0] + (lo ? p.a_tx_bytes[1] : 0));
+      if (leader)
+        ptx::mbar_arrive_expect_tx(s.afull, 2 * (p.a_tx_bytes[0] + (lo ? p.a_tx_bytes[1] : 0)));
       for (int part = 0; part < (lo ? 2 : 1); ++part) {
         for (int c = 0; c < p.nchunk; ++c) {
           const int w = p.chunk_w[c];
-          ptx::tma_load_2d(s.base + p.a_off[part][c], pick_map(w, &maps.a64, &maps.a32, &maps.a16),
-                           part * p.dp + p.chunk_x[c], it.qt * kTileQ, s.afull);
+          ptx::tma_load_2d_pair(s.base + p.a_off[part][c],
+                                pick_map(w, &maps.a64, &maps.a32, &maps.a16),
+                                part * p.dp + p.chunk_x[c], it.qt * kTileQ, afull_l);
         }
       }
       ++a_loads;
@@ -124,34 +154,48 @@ __device__ void run_producer(const FusedParams& p, const FusedMaps& maps, const 
       ptx::bulk_load(slot_side + kSideIdOff, p.row_id + pos0, 1024, &s.side_full[sb]);
       if (p.allow) ptx::bulk_load(slot_side + kSideAllowOff, p.allow + pos0 / 32, 32, &s.side_full[sb]);
       ++tile;
-      for (int u = 0; u < p.nunits; ++u) {
-        const uint32_t slot = unit % p.nstages;
-        const uint32_t use = unit / p.nstages;
-        if (use > 0 &&
-            !ptx::mbar_wait(&s.empty[slot], (use - 1) & 1, s.abort, p.err, kErrWaitSlotEmpty)) {
-          ok = false;
-          break;
+      // Units in MMA order: database part bp major, chunk c minor. The chunk loop is unrolled so
+      // the per-chunk parameters are static-index loads, and the ring position is tracked
+      // without division (like the MMA thread's).
+      const int row = t * p.tile_stride * kTileN + static_cast<int>(rank) * kHalfN;
+      for (int bp = 0; bp < p.b_parts && ok; ++bp) {
+#pragma unroll
+        for (int c = 0; c < kMaxChunks; ++c) {
+          if (c >= p.nchunk) break;
+          if (wrapped &&
+              !ptx::mbar_wait(&s.empty[slot], phase ^ 1u, s.abort, p.err, kErrWaitSlotEmpty)) {
+            ok = false;
+            break;
+          }
+          const int w = p.chunk_w[c];
+          if (leader)
+            ptx::mbar_arrive_expect_tx(&s.full[slot], static_cast<uint32_t>(kTileN * w * 2));
+          ptx::tma_load_2d_pair(s.base + p.stage_off + slot * kUnitBytes,
+                                pick_map(w, &maps.b64, &maps.b32, &maps.b16),
+                                bp * p.dp + p.chunk_x[c], row, full_l + slot * 8);
+          ++unit;
+          if (++slot == static_cast<uint32_t>(p.nstages)) {
+            slot = 0;
+            phase ^= 1u;
+            wrapped = true;
+          }
         }
-        const int bp = u / p.nchunk, c = u % p.nchunk, w = p.chunk_w[c];
-        ptx::mbar_arrive_expect_tx(&s.full[slot], static_cast<uint32_t>(kTileN * w * 2));
-        ptx::tma_load_2d(s.base + p.stage_off + slot * kUnitBytes,
-                         pick_map(w, &maps.b64, &maps.b32, &maps.b16), bp * p.dp + p.chunk_x[c],
-                         t * p.tile_stride * kTileN, &s.full[slot]);
-        ++unit;
       }
     }
   }
-  // Unwind: every load this thread issued must land before the CTA exits. The last load into
-  // each slot completes the phase (use & 1) of that slot's full barrier.
+  // Unwind: every copy this thread issued must have landed before the CTA exits. B copies count
+  // on the leader's barriers, so this CTA waits for their consumption instead: the MMA commit
+  // that frees the last use of each slot (empty, phase of that use), and the final MMA
+  // completion for the query tile. Side copies count on this CTA's own barriers.
   const uint32_t issued = unit;
   for (uint32_t slot = 0; slot < static_cast<uint32_t>(p.nstages) && slot < issued; ++slot) {
     const uint32_t last = ((issued - 1 - slot) / p.nstages) * p.nstages + slot;
-    drain_wait(&s.full[slot], (last / p.nstages) & 1, p.err);
+    drain_wait(&s.empty[slot], (last / p.nstages) & 1, p.err, s.abort);
   }
-  if (a_loads > 0) drain_wait(s.afull, (a_loads - 1) & 1, p.err);
+  if (a_loads > 0) drain_wait(s.drain, 0, p.err, s.abort);
   for (uint32_t sb = 0; sb < static_cast<uint32_t>(kSideBufs) && sb < tile; ++sb) {
     const uint32_t last = ((tile - 1 - sb) / kSideBufs) * kSideBufs + sb;
-    drain_wait(&s.side_full[sb], (last / kSideBufs) & 1, p.err);
+    drain_wait(&s.side_full[sb], (last / kSideBufs) & 1, p.err, s.abort);
   }
 }
 
@@ -166,7 +210,7 @@ __device__ void run_producer(const FusedParams& p, const FusedMaps& maps, const 
 // run_mma_dispatch picks the instance once per launch. Descriptors are built once per chunk and
 // kept in registers (the chunk loop is unrolled over kMaxChunks so every index is static); the
 // ring position is tracked without division.
-constexpr uint32_t kIdesc = ptx::idesc_f16_f32(kTileQ, kTileN);
+constexpr uint32_t kIdesc = ptx::idesc_f16_f32(kPairQ, kTileN);
 // Descriptor address fields count 16-byte units; a K step of 16 fp16 values is 32 bytes.
 constexpr uint64_t kStepDesc = 32 >> 4;
 constexpr uint64_t kSlotDesc = kUnitBytes >> 4;
@@ -176,12 +220,12 @@ constexpr uint64_t kSlotDesc = kUnitBytes >> 4;
 template <bool LO, int KS>
 __device__ __forceinline__ void issue_unit(uint32_t d_tmem, uint64_t a_hi, uint64_t a_lo,
                                            uint64_t bd, uint32_t acc) {
-  ptx::mma_f16_ss(d_tmem, a_hi, bd, kIdesc, acc);
-  if constexpr (LO) ptx::mma_f16_ss(d_tmem, a_lo, bd, kIdesc, 1);
+  ptx::mma_f16_pair(d_tmem, a_hi, bd, kIdesc, acc);
+  if constexpr (LO) ptx::mma_f16_pair(d_tmem, a_lo, bd, kIdesc, 1);
 #pragma unroll
   for (int ks = 1; ks < KS; ++ks) {
-    ptx::mma_f16_ss(d_tmem, a_hi + ks * kStepDesc, bd + ks * kStepDesc, kIdesc, 1);
-    if constexpr (LO) ptx::mma_f16_ss(d_tmem, a_lo + ks * kStepDesc, bd + ks * kStepDesc, kIdesc, 1);
+    ptx::mma_f16_pair(d_tmem, a_hi + ks * kStepDesc, bd + ks * kStepDesc, kIdesc, 1);
+    if constexpr (LO) ptx::mma_f16_pair(d_tmem, a_lo + ks * kStepDesc, bd + ks * kStepDesc, kIdesc, 1);
   }
 }
 
@@ -202,23 +246,21 @@ __device__ __forceinline__ void issue_chunk(uint32_t d_tmem, uint64_t a_hi, uint
 template <bool LO, int KS>
 __device__ void run_mma(const FusedParams& p, const Smem& s, uint32_t tmem_base) {
   const uint32_t base_addr = ptx::smem_addr(s.base);
-  uint64_t a_hi[kMaxChunks], a_lo[kMaxChunks], b_base[kMaxChunks];
-  int ksteps[kMaxChunks];
-#pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
-    const int w = c < p.nchunk ? p.chunk_w[c] : 16;
-    const uint32_t row_bytes = static_cast<uint32_t>(w * 2);
-    a_hi[c] = ptx::smem_desc(base_addr + p.a_off[0][c], row_bytes);
-    a_lo[c] = ptx::smem_desc(base_addr + p.a_off[1][c], row_bytes);
-    b_base[c] = ptx::smem_desc(base_addr + p.stage_off, row_bytes);
-    ksteps[c] = w / 16;
-  }
+  // Equal chunk widths (KS > 0): the chunks' query regions are evenly spaced, so descriptors are
+  // a base plus a constant per chunk (three registers). Mixed widths (KS == 0): each chunk's
+  // descriptors are rebuilt at use from the kernel parameters (static indices after unrolling),
+  // which keeps them out of registers.
+  constexpr uint64_t kAStep = KS > 0 ? static_cast<uint64_t>(kTileQ * 32 * KS) >> 4 : 0;
+  constexpr uint32_t kRowBytes = KS > 0 ? 32 * KS : 0;
+  const uint64_t a_hi0 = ptx::smem_desc(base_addr + p.a_off[0][0], kRowBytes ? kRowBytes : 128);
+  const uint64_t a_lo0 = ptx::smem_desc(base_addr + p.a_off[1][0], kRowBytes ? kRowBytes : 128);
+  const uint64_t b0 = ptx::smem_desc(base_addr + p.stage_off, kRowBytes ? kRowBytes : 128);
   uint32_t slot = 0, phase = 0;
   uint32_t tile = 0;
   int a_waits = 0, cur_qt = -1;
   bool ok = true;
-  for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
-    const Item it = item_of(p, item);
+  for (int item = first_item(); item < p.num_items && ok; item += item_step()) {
+    const Item it = item_of(p, item, 0);
     if (it.qt != cur_qt) {
       if (!ptx::mbar_wait(s.afull, a_waits & 1, s.abort, p.err, kErrWaitA)) {
         ok = false;
@@ -249,13 +291,25 @@ __device__ void run_mma(const FusedParams& p, const Smem& s, uint32_t tmem_base)
             break;
           }
           ptx::tc_fence_after();
-          const uint64_t bd = b_base[c] + slot * kSlotDesc;
+          uint64_t ah, al, bd;
+          int ksteps = KS;
+          if constexpr (KS > 0) {
+            ah = a_hi0 + c * kAStep;
+            al = a_lo0 + c * kAStep;
+            bd = b0 + slot * kSlotDesc;
+          } else {
+            const uint32_t row_bytes = static_cast<uint32_t>(p.chunk_w[c] * 2);
+            ah = ptx::smem_desc(base_addr + p.a_off[0][c], row_bytes);
+            al = ptx::smem_desc(base_addr + p.a_off[1][c], row_bytes);
+            bd = ptx::smem_desc(base_addr + p.stage_off + slot * kUnitBytes, row_bytes);
+            ksteps = p.chunk_w[c] / 16;
+          }
           if (LO && bp == 0)
-            issue_chunk<true, KS>(d_tmem, a_hi[c], a_lo[c], bd, acc, ksteps[c]);
+            issue_chunk<true, KS>(d_tmem, ah, al, bd, acc, ksteps);
           else
-            issue_chunk<false, KS>(d_tmem, a_hi[c], a_lo[c], bd, acc, ksteps[c]);
+            issue_chunk<false, KS>(d_tmem, ah, al, bd, acc, ksteps);
           acc = 1;
-          ptx::mma_commit(&s.empty[slot]);  // slot reusable once these MMAs have read it
+          ptx::mma_commit_pair(&s.empty[slot]);  // both CTAs' slot reusable once read
           if (++slot == static_cast<uint32_t>(p.nstages)) {
             slot = 0;
             phase ^= 1u;
@@ -263,16 +317,17 @@ __device__ void run_mma(const FusedParams& p, const Smem& s, uint32_t tmem_base)
         }
       }
       if (!ok) break;
-      ptx::mma_commit(&s.tfull[buf]);
+      ptx::mma_commit_pair(&s.tfull[buf]);
       ++tile;
     }
     if (!ok) break;
-    const int next = item + gridDim.x;
-    if (next < p.num_items && item_of(p, next).qt != it.qt) ptx::mma_commit(s.aempty);
+    const int next = item + item_step();
+    if (next < p.num_items && item_of(p, next, 0).qt != it.qt) ptx::mma_commit_pair(s.aempty);
   }
-  // Unwind: wait until every MMA issued by this thread has completed before TMEM is released.
-  ptx::mma_commit(s.drain);
-  drain_wait(s.drain, 0, p.err);
+  // Unwind: every MMA issued by this thread completes before either CTA releases TMEM or shared
+  // memory (both CTAs wait for `drain`).
+  ptx::mma_commit_pair(s.drain);
+  drain_wait(s.drain, 0, p.err, s.abort);
 }
 
 // Picks the run_mma instance: LO from the launch's query-split flag, KS from the chunk widths
@@ -473,31 +528,36 @@ __device__ __forceinline__ void slow_path(const FusedParams& p, const float (&r)
   }
 }
 
-template <int KL>
-__device__ __forceinline__ void process_chunk(const FusedParams& p, const float (&r)[32],
-                                              int64_t col0, int ct0, const uint8_t* side,
-                                              EpiState<KL>& st) {
-  const float g = max32(r);
-  if (!(g < st.thr)) slow_path<KL>(p, r, col0, ct0, side, st);
-  __syncwarp();  // tcgen05.ld / wait::ld are warp-collective: reconverge after the slow path
-}
 
 template <int KL>
-__device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_base) {
+__device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_base, uint32_t rank) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int quarter = warp & 3, half = warp >> 2;
+  // TMEM buffers are handed back to the leader's MMA thread: its tempty barrier counts the
+  // arrivals of both CTAs' epilogue warps.
+  const uint32_t tempty_l = ptx::peer_addr(s.tempty, 0);
+  // Warp w reads TMEM lane quarter w % 4 (the hardware ties a warp to its quarter) and owns
+  // columns [kPartCols * part, kPartCols * part + kPartCols) of every tile, part = w / 4.
+  const int quarter = warp & 3, part = warp >> 2;
+  constexpr int nchunks = kPartCols / 32;
+  float* my_row = s.defer + threadIdx.x * kDeferStride;  // this lane's deferred chunk
   const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
   uint32_t tile = 0;
   EpiState<KL> st;
-  for (int item = blockIdx.x; item < p.num_items; item += gridDim.x) {
-    const Item it = item_of(p, item);
+  for (int item = first_item(); item < p.num_items; item += item_step()) {
+    const Item it = item_of(p, item, rank);
     const int64_t q = static_cast<int64_t>(it.qt) * kTileQ + quarter * 32 + lane;
     st.m = p.q_mul[q];
     st.inv_m = 1.0f / st.m;
     st.real = q < p.nq;
     st.qi = q;
-    // Aux ranges are loaded one tile ahead.
-    float2 ta_next = p.tile_aux[it.t0 * p.tile_stride];
+    // The filter threshold is computed against the aux range of the tile's group of
+    // kGroupTiles consecutive tiles (rows are sorted by aux, so the group range is barely wider
+    // than a tile's, and it stays conservative). It is therefore recomputed only when the group
+    // changes, when the shared bound is re-read, or after an insertion, not on every tile. The
+    // next group's range is loaded one tile before it is needed.
+    int g_cur = (it.t0 * p.tile_stride) >> kGroupShift, g_pf = -1;
+    float2 ta_pf = make_float2(0.f, 0.f);
+    st.ta = p.group_aux[g_cur];
     if constexpr (KL > 0) {
       read_bound<KL>(p, q, st);
 #pragma unroll
@@ -509,23 +569,34 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
     // t-1 is done, so it is prepared then, while the next TMEM buffer is still being filled:
     // after the buffer fills, this warp goes straight to reading it and hands it back sooner,
     // which is what lets the MMA of tile t+2 start before the tensor core runs dry.
-    auto prepare = [&](int t) {
-      const int tile_pos = t * p.tile_stride;
-      st.ta = ta_next;
-      if (t + 1 < it.t1) ta_next = p.tile_aux[tile_pos + p.tile_stride];
+    auto prepare = [&](int t, bool refresh) {
+      const int g = (t * p.tile_stride) >> kGroupShift;
+      if (g != g_cur) {
+        st.ta = g == g_pf ? ta_pf : p.group_aux[g];
+        g_cur = g;
+        refresh = true;
+      }
+      if (t + 1 < it.t1) {
+        const int gn = ((t + 1) * p.tile_stride) >> kGroupShift;
+        if (gn != g_cur && gn != g_pf) {
+          ta_pf = p.group_aux[gn];
+          g_pf = gn;
+        }
+      }
       if constexpr (KL > 0) {
         if (((t - it.t0) & (kBoundPeriod - 1)) == kBoundPeriod - 1 && st.real) {
           publish_bound<KL>(p, q, st);
           read_bound<KL>(p, q, st);
+          refresh = true;
         }
-      } else {
+      } else if (refresh) {
         const float tv = keys::key_value(st.gkey);
         st.by_key = p.app_exact || !(tv < kInf);
         st.gw = st.by_key ? tv : append_limit(tv, st.ta);
       }
-      refresh_threshold<KL>(st, p.rank_kind);
+      if (refresh) refresh_threshold<KL>(st, p.rank_kind);
     };
-    prepare(it.t0);
+    prepare(it.t0, true);
     bool ok = true;
     for (int t = it.t0; t < it.t1; ++t) {
       const uint32_t buf = tile & 1, use = tile >> 1;
@@ -540,56 +611,64 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
       }
       ptx::tc_fence_after();
       const uint8_t* side = s.side + sb * kSideBytes;
-      const int ct0 = half * 128;  // this warp's first column within the tile
+      const int ct0 = part * kPartCols;  // this warp's first column within the tile
       const int tile_pos = t * p.tile_stride;
-      const uint32_t taddr = lane_base + buf * kTileN + half * 128;
-      const int64_t col0 = static_cast<int64_t>(tile_pos) * kTileN + half * 128;
-      // Two chunks in flight at a time (one for 32-entry lists: register budget of 168 at 320
-      // threads); the other warp of this lane quarter overlaps its loads with this one's work.
-      float r0[32], r1[32];
-      if constexpr (KL >= 32) {
-        ptx::tmem_ld32(taddr, r0);
+      const uint32_t taddr = lane_base + buf * kTileN + ct0;
+      const int64_t col0 = static_cast<int64_t>(tile_pos) * kTileN + ct0;
+      // One 32-column chunk in registers at a time, a 3-input max tree against the threshold.
+      // A lane whose chunk may hold a candidate saves it to its deferred row (the first such
+      // chunk of the tile) or flags it (any further one: item starts, lists still empty). The
+      // exact checks run after the loop: flagged chunks first, re-read from TMEM while the
+      // buffer is still held; then the buffer goes back to the MMA, then the deferred row.
+      uint32_t flagged = 0;  // chunks this lane must re-read
+      int saved = -1;        // chunk index in the deferred row, or -1
+#pragma unroll
+      for (int c = 0; c < nchunks; ++c) {
+        float r0[32];
+        ptx::tmem_ld32(taddr + 32 * c, r0);
         ptx::tmem_wait_ld();
-        process_chunk<KL>(p, r0, col0, ct0, side, st);
-        ptx::tmem_ld32(taddr + 32, r0);
-        ptx::tmem_wait_ld();
-        process_chunk<KL>(p, r0, col0 + 32, ct0 + 32, side, st);
-        ptx::tmem_ld32(taddr + 64, r0);
-        ptx::tmem_wait_ld();
-        process_chunk<KL>(p, r0, col0 + 64, ct0 + 64, side, st);
-        ptx::tmem_ld32(taddr + 96, r0);
-        ptx::tmem_wait_ld();
-      } else {
-        ptx::tmem_ld32(taddr, r0);
-        ptx::tmem_ld32(taddr + 32, r1);
-        ptx::tmem_wait_ld();
-        process_chunk<KL>(p, r0, col0, ct0, side, st);
-        process_chunk<KL>(p, r1, col0 + 32, ct0 + 32, side, st);
-        ptx::tmem_ld32(taddr + 64, r0);
-        ptx::tmem_ld32(taddr + 96, r1);
-        ptx::tmem_wait_ld();
+        if (!(max32(r0) < st.thr)) {
+          if (saved < 0) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) my_row[j] = r0[j];
+            saved = c;
+          } else {
+            flagged |= 1u << c;
+          }
+        }
+        __syncwarp();
       }
-      // This warp's 128 columns are in registers: hand its share of the buffer back.
+      if (__any_sync(0xffffffffu, flagged != 0)) {
+        for (int c = 0; c < nchunks; ++c) {
+          if (!__any_sync(0xffffffffu, (flagged >> c) & 1u)) continue;
+          float r0[32];
+          ptx::tmem_ld32(taddr + 32 * c, r0);
+          ptx::tmem_wait_ld();
+          if ((flagged >> c) & 1u) slow_path<KL>(p, r0, col0 + 32 * c, ct0 + 32 * c, side, st);
+          __syncwarp();
+        }
+      }
+      // Every chunk of this warp is read: hand its share of the buffer back.
       ptx::tc_fence_before();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&s.tempty[buf]);
-      if constexpr (KL >= 32) {
-        process_chunk<KL>(p, r0, col0 + 96, ct0 + 96, side, st);
-      } else {
-        process_chunk<KL>(p, r0, col0 + 64, ct0 + 64, side, st);
-        process_chunk<KL>(p, r1, col0 + 96, ct0 + 96, side, st);
+      if (lane == 0) ptx::mbar_arrive_cluster(tempty_l + buf * 8);
+      if (saved >= 0) {
+        float r0[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r0[j] = my_row[j];
+        slow_path<KL>(p, r0, col0 + 32 * saved, ct0 + 32 * saved, side, st);
       }
       // Side slot released once this warp's exact checks of the tile are done.
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&s.side_empty[sb]);
       ++tile;
-      if (t + 1 < it.t1) prepare(t + 1);
+      if (t + 1 < it.t1) prepare(t + 1, false);
     }
     if (!ok) return;
     if constexpr (KL > 0) {
       if (st.real) publish_bound<KL>(p, q, st);
       uint64_t* dst =
-          p.out + ((static_cast<size_t>(q) * p.num_sc + it.sc) * kListsPerItem + half) * KL;
+          p.out + ((static_cast<size_t>(q) * p.num_sc + it.sc) * kListsPerItem + part) * KL;
 #pragma unroll
       for (int i = 0; i < KL; ++i) dst[i] = st.L[i];
     }
@@ -597,11 +676,12 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
 }
 
 template <int KL>
-__global__ void __launch_bounds__(kFusedThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFusedThreads, 1)
     knn_fused_kernel(const __grid_constant__ FusedMaps maps, const __grid_constant__ FusedParams p) {
   extern __shared__ uint8_t smem_raw[];
   const Smem s = carve(p, smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = ptx::cluster_rank();
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < p.nstages; ++i) {
@@ -610,7 +690,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       ptx::mbar_init(&s.tfull[i], 1);
-      ptx::mbar_init(&s.tempty[i], kEpiWarps);
+      ptx::mbar_init(&s.tempty[i], 2 * kEpiWarps);  // leader's: both CTAs' epilogue warps
     }
     ptx::mbar_init(s.afull, 1);
     ptx::mbar_init(s.aempty, 1);
@@ -626,27 +706,35 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     ptx::tma_prefetch_desc(&maps.a64);
     ptx::tma_prefetch_desc(&maps.b64);
   }
-  if (warp == kEpiWarps + 1) ptx::tmem_alloc(s.tmem_slot, kTmemCols);
+  if (warp == kEpiWarps + 1) ptx::tmem_alloc_pair(s.tmem_slot, kTmemCols);
+  // Both CTAs' barriers are initialised (and TMEM allocated) before either CTA touches the
+  // other's barriers or shared memory.
   ptx::tc_fence_before();
-  __syncthreads();
+  ptx::cluster_sync();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *s.tmem_slot;
   const bool lo = p.query_split != 0 && *p.q_lo_flag != 0;
 
   if (warp == kEpiWarps) {
-    if (lane == 0) run_producer(p, maps, s, lo);
+    if (lane == 0) run_producer(p, maps, s, lo, rank);
   } else if (warp == kEpiWarps + 1) {
-    if (lane == 0) run_mma_dispatch(p, s, tmem_base, lo);
+    if (lane == 0) {
+      if (rank == 0)
+        run_mma_dispatch(p, s, tmem_base, lo);
+      else  // the leader's MMAs read this CTA's shared memory and write its TMEM
+        drain_wait(s.drain, 0, p.err, s.abort);
+    }
     __syncwarp();
   } else {
-    run_epilogue<KL>(p, s, tmem_base);
+    run_epilogue<KL>(p, s, tmem_base, rank);
   }
 
+  // Neither CTA leaves (or frees TMEM) while the other may still arrive on its barriers.
   ptx::tc_fence_before();
-  __syncthreads();
+  ptx::cluster_sync();
   if (warp == kEpiWarps + 1) {
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem_base, kTmemCols);
+    ptx::tmem_dealloc_pair(tmem_base, kTmemCols);
   }
 }
 
@@ -661,6 +749,31 @@ cudaError_t launch_kl(const FusedMaps& maps, const FusedParams& p, int grid, cud
 
 }  // namespace
 
+int fused_max_pairs(int smem_bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<int, int>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 1;
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_pair(dev, smem_bytes);
+  auto hit = cache.find(key);
+  if (hit != cache.end()) return hit->second;
+  auto kern = knn_fused_kernel<16>;  // every instance has the same threads, smem and cluster shape
+  int pairs = 0;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) ==
+      cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(kFusedThreads, 1, 1);
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem_bytes);
+    if (cudaOccupancyMaxActiveClusters(&pairs, kern, &cfg) != cudaSuccess) pairs = 0;
+  }
+  (void)cudaGetLastError();
+  if (pairs < 1) pairs = 1;
+  cache[key] = pairs;
+  return pairs;
+}
+
 bool plan_fused_smem(FusedParams& p, int max_smem_optin) {
   int off = 0;
   for (int part = 0; part < 2; ++part) {
@@ -673,11 +786,14 @@ bool plan_fused_smem(FusedParams& p, int max_smem_optin) {
     }
   }
   p.side_off = off;
-  off += (kSideBufs * kSideBytes + 1023) & ~1023;  // stages stay 1024-aligned (128B swizzle)
+  off += kSideBufs * kSideBytes;
+  p.defer_off = off;
+  off += kEpiWarps * 32 * kDeferStride * 4;
+  off = (off + 1023) & ~1023;  // stages stay 1024-aligned (128-byte swizzle)
   p.stage_off = off;
   const int budget = max_smem_optin - 1024;  // alignment slack
   auto bar_bytes = [](int stages) { return (2 * stages + 7 + 2 * kSideBufs) * 8 + 16; };
-  int stages = 8;
+  int stages = kMaxStages;
   for (; stages >= 2; --stages) {
     if (off + stages * kUnitBytes + bar_bytes(stages) <= budget) break;
   }

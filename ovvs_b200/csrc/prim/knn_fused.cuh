@@ -2,21 +2,30 @@
 //
 // Replaces the reference's dense pairwise + top-k pipeline (src/prim/mixer.cpp:843-864 with
 // prim_pairwise 174-221 and cpu_topk src/prim/cpu/cpu_prims.cpp:61-106): the nq x n score matrix
-// never exists. One CTA per SM loops over work items (query tile of 128, super-chunk of database
-// tiles of 256 rows):
+// never exists. CTAs work in pairs (clusters of 2, one CTA per SM): a pair loops over work items
+// (query pair-tile of 256 = 128 per CTA, super-chunk of database tiles of 256 rows) and shares
+// one tcgen05 MMA of M=256 x N=256, so each SM stores and reads only half of every database tile
+// (halving each SM's share of the database traffic and of the MMA instruction stream):
 //
-//   warp 8  TMA producer   loads the query tile once per item (resident A) and streams database
-//                          K-chunks (<= 64 fp16 columns x 256 rows) through an smem ring, plus
-//                          per tile the rows' aux values, ids and allow bits (2 KB) into a
-//                          4-deep side ring that the epilogue reads on its exact path;
-//   warp 9  MMA issuer     tcgen05.mma kind::f16, M=128 (queries) x N=256 (rows), fp32
-//                          accumulators in TMEM, double-buffered (2 x 256 columns);
-//   warps 0-7 epilogue     warps w and w+4 share TMEM lane quarter w (32 queries, one per
-//                          thread) and take 128 of the 256 columns each: four tcgen05.ld of 32
-//                          columns issued back to back, one wait, then per 32 columns a 3-input
-//                          max tree against the query's current threshold and, rarely, an exact
-//                          per-column check + insertion into the thread's sorted register list
-//                          of the KL best (value, row id) keys. Each half keeps its own list.
+//   warp 8  TMA producer   (each CTA) loads its 128 queries once per item (resident A) and
+//                          streams its 128-row half of each database K-chunk (<= 64 fp16
+//                          columns) through an smem ring, completion counted on the leader
+//                          CTA's barriers; plus per tile the 256 rows' aux values, ids and
+//                          allow bits (2 KB) into a 4-deep side ring that its epilogue reads
+//                          on the exact path;
+//   warp 9  MMA issuer     (leader CTA only) tcgen05.mma.cta_group::2 kind::f16, M=256 x N=256,
+//                          fp32 accumulators in both CTAs' TMEM (each CTA: its 128 queries x
+//                          the 256 rows), double-buffered (2 x 256 columns);
+//   warps 0-7 epilogue     warps w, w+4 share TMEM lane quarter w % 4 (32 queries, one per
+//                          thread) and take columns [0,128) and [128,256): per 32
+//                          columns one tcgen05.ld and a 3-input max tree against the query's
+//                          current threshold. A lane whose chunk may hold a candidate (about 3%
+//                          of chunks) copies it to its private deferred row in shared memory;
+//                          the exact per-column checks + insertions into the thread's sorted
+//                          register list of the KL best (value, row id) keys run after the
+//                          TMEM buffer is handed back, so with 16 epilogue warps per pair tile
+//                          the MMA never waits for the slowest one. Each column part keeps its
+//                          own list.
 //
 // Ranking values ("v", smaller is better) per query q and database position j, from the MMA dot
 // product s (queries and rows pre-scaled by powers of two, split into fp16 hi/lo parts when the
@@ -38,12 +47,16 @@
 namespace ovvs {
 namespace prim {
 
-constexpr int kTileQ = 128;                // queries per tile: MMA M, TMEM lanes
+constexpr int kTileQ = 128;                // queries per CTA tile: TMEM lanes
+constexpr int kPairQ = 2 * kTileQ;         // queries per pair tile: MMA M
 constexpr int kTileN = 256;                // database rows per tile: MMA N
-constexpr int kUnitBytes = kTileN * 128;   // one smem slot: a 64-column fp16 chunk of a tile
-constexpr int kEpiWarps = 8;               // two warps per TMEM lane quarter, 128 columns each
-constexpr int kListsPerItem = 2;           // list-mode output: one sorted list per column half
-constexpr int kFusedThreads = 320;         // warps 0-7 epilogue, 8 TMA, 9 MMA
+constexpr int kHalfN = kTileN / 2;         // rows of each tile held by one CTA of the pair
+constexpr int kUnitBytes = kHalfN * 128;   // one smem slot: a 64-column fp16 chunk, 128 rows
+constexpr int kEpiWarps = 8;               // two warps per TMEM lane quarter
+constexpr int kPartCols = 128;             // columns per epilogue warp (a part of the tile)
+constexpr int kListsPerItem = kEpiWarps / 4;  // list-mode output: one sorted list per column part
+constexpr int kFusedThreads = 32 * (kEpiWarps + 2);  // epilogue warps, then TMA, then MMA
+constexpr int kMaxStages = 16;             // smem ring slots at most
 constexpr int kMaxChunks = 8;              // padded dim <= 512 per part
 constexpr int kTmemCols = 512;             // two 256-column fp32 accumulators
 constexpr int kSideBufs = 4;               // side ring depth (tiles)
@@ -51,6 +64,8 @@ constexpr int kSideAuxOff = 0;             // side slot: aux[256] fp32
 constexpr int kSideIdOff = 1024;           //            row id[256] u32
 constexpr int kSideAllowOff = 2048;        //            allow bits[256] (8 words)
 constexpr int kSideBytes = 2176;           // slot stride (multiple of 128 bytes)
+constexpr int kDeferStride = 33;           // floats per deferred row (32 values + chunk index;
+                                           // 33 keeps the lanes' rows on distinct banks)
 
 enum RankKind : int { kRankAffine = 0, kRankScaled = 1, kRankColumnScaled = 2 };
 
@@ -80,18 +95,20 @@ struct FusedParams {
   int nstages;                     // smem ring slots
   int stage_off;                   // smem byte offset of slot 0
   int side_off;                    // smem byte offset of the side ring
+  int defer_off;                   // smem byte offset of the epilogue's deferred rows
   int bar_off;                     // smem byte offset of the mbarriers
   int smem_bytes;                  // dynamic smem requested (includes 1 KB alignment slack)
   int query_split;                 // 1: the query lo part is used when *q_lo_flag != 0
   const int* q_lo_flag;            // set by the query-prep kernel
-  int num_qtiles;
+  int num_qtiles;                  // 128-query tiles (even: queries are padded to kPairQ)
   int num_dbtiles;
   int tiles_per_item;
-  int num_sc;                      // super-chunks (items per query tile)
-  int num_items;
+  int num_sc;                      // super-chunks (items per query pair-tile)
+  int num_items;                   // fused_items(num_qtiles, num_sc)
   int64_t n_rows;                  // valid database rows (positions >= n_rows are padding)
   const float* row_aux;            // [n_pad] aux by position
-  const float2* tile_aux;          // [num_dbtiles] (min, max) of aux over the tile's valid rows
+  const float2* group_aux;         // (min, max) of aux per group of 8 consecutive tiles (by
+                                   // position: group of tile t = (t * tile_stride) >> 3)
   const uint32_t* row_id;          // [n_pad] position -> row id
   const float* q_mul;              // [q_pad] m_q
   const uint32_t* allow;           // [n_pad / 32] allow bits by position, or null
@@ -99,8 +116,8 @@ struct FusedParams {
   int64_t nq;                      // real queries (lanes >= nq are padding and never select)
   int k_pub;                       // rank (1-based) whose key a list publishes as a bound
   uint64_t* q_bound;               // [q_pad] smallest published k_pub-th key per query
-  uint64_t* out;                   // [q_pad][num_sc][2][KL] sorted keys (list mode; one list per
-                                   // column half)
+  uint64_t* out;                   // [q_pad][num_sc][kListsPerItem][KL] sorted keys (list mode;
+                                   // one list per column part)
   int* err;                        // watchdog word
   int tile_stride = 1;             // item tile ranges count every tile_stride-th database tile
   // Append mode (KL = 0): every column whose key is within the query's bound q_tau_key[q] is
@@ -123,13 +140,27 @@ constexpr int kBoundPeriod = 16;
 
 struct FusedMaps {
   CUtensorMap a64, a32, a16;  // queries [q_pad, 2 * dp] fp16, boxes {64|32|16, 128}
-  CUtensorMap b64, b32, b16;  // rows    [n_pad, b_parts * dp] fp16, boxes {64|32|16, 256}
+  CUtensorMap b64, b32, b16;  // rows    [n_pad, b_parts * dp] fp16, boxes {64|32|16, 128}
 };
 
+// Query rows are padded to whole pair tiles.
+inline int64_t pad_queries(int64_t nq) { return (nq + kPairQ - 1) / kPairQ * kPairQ; }
+// Work items: query pair-tiles x super-chunks.
+inline int fused_items(int num_qtiles, int num_sc) { return num_qtiles / 2 * num_sc; }
+// Grid: one CTA pair per two SMs, at most one pair per item.
+inline int fused_grid(int num_items, int num_sms) {
+  const int pairs = num_items < num_sms / 2 ? num_items : num_sms / 2;
+  return 2 * (pairs > 0 ? pairs : 1);
+}
+
 // Host-side launcher (knn_fused.cu). `kl` in {4, 8, 16, 32} (sorted register lists), or 0 for
-// append mode.
+// append mode. `grid` is even (clusters of 2).
 cudaError_t launch_knn_fused(const FusedMaps& maps, const FusedParams& p, int kl, int grid,
                              cudaStream_t stream);
+
+// CTA pairs of the fused kernel that can be resident at once on the current device with
+// `smem_bytes` of dynamic shared memory per CTA (a pair needs two SMs of one GPC). Cached.
+int fused_max_pairs(int smem_bytes);
 
 // Fills the smem layout fields of `p` (offsets, stages) for dim `dp` split into chunks.
 // Returns false if the query tile does not fit in shared memory.

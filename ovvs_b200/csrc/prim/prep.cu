@@ -188,6 +188,20 @@ __global__ void tile_bounds_kernel(const float* __restrict__ aux, int64_t n, int
   tile_aux[t] = make_float2(lo, hi);
 }
 
+__global__ void group_bounds_kernel(const float2* __restrict__ tile_aux, int num_tiles,
+                                    float2* __restrict__ group_aux) {
+  const int g = blockIdx.x * blockDim.x + threadIdx.x;
+  const int t0 = g * kGroupTiles;
+  if (t0 >= num_tiles) return;
+  const int t1 = min(num_tiles, t0 + kGroupTiles);
+  float2 r = tile_aux[t0];
+  for (int t = t0 + 1; t < t1; ++t) {
+    r.x = fminf(r.x, tile_aux[t].x);
+    r.y = fmaxf(r.y, tile_aux[t].y);
+  }
+  group_aux[g] = r;
+}
+
 __global__ void allow_bits_kernel(const uint8_t* __restrict__ bitset, int64_t row_offset,
                                   const uint32_t* __restrict__ row_id, int64_t n, int64_t n_pad,
                                   uint32_t* __restrict__ allow_pos) {
@@ -238,6 +252,9 @@ void launch_scatter_rows(const void* data, int dtype, int64_t n, int64_t n_pad, 
 void launch_tile_bounds(const float* aux, int64_t n, int num_tiles, float2* tile_aux,
                         cudaStream_t stream) {
   tile_bounds_kernel<<<(num_tiles + 127) / 128, 128, 0, stream>>>(aux, n, num_tiles, tile_aux);
+  const int groups = (num_tiles + kGroupTiles - 1) / kGroupTiles;
+  group_bounds_kernel<<<(groups + 127) / 128, 128, 0, stream>>>(tile_aux, num_tiles,
+                                                                tile_aux + num_tiles);
 }
 
 void launch_allow_bits(const uint8_t* bitset, int64_t row_offset, const uint32_t* row_id,

@@ -63,7 +63,13 @@ void launch_scatter_rows(const void* data, int dtype, int64_t n, int64_t n_pad, 
                          float* exact32, float* aux, float* norm_sorted, uint32_t* row_id,
                          uint32_t* inv_perm, cudaStream_t stream);
 
-// tile_aux[t] = (min, max) of aux over valid positions of tile t (256 rows).
+// tile_aux[t] = (min, max) of aux over valid positions of tile t (256 rows), for t < num_tiles,
+// followed by the same range per group of kGroupTiles consecutive tiles:
+// tile_aux[num_tiles + g] covers tiles [g * kGroupTiles, (g + 1) * kGroupTiles). The buffer holds
+// num_tiles + ceil(num_tiles / kGroupTiles) entries.
+constexpr int kGroupTiles = 8;
+constexpr int kGroupShift = 3;
+inline int group_count(int num_tiles) { return (num_tiles + kGroupTiles - 1) / kGroupTiles; }
 void launch_tile_bounds(const float* aux, int64_t n, int num_tiles, float2* tile_aux,
                         cudaStream_t stream);
 
