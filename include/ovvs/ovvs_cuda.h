@@ -35,6 +35,23 @@ OVVS_API ovvsStatus ovvsResourcesDevice(ovvsResources_t res, int32_t* device);
 OVVS_API ovvsStatus ovvsResourcesSetProfiling(ovvsResources_t res, int32_t enable);
 OVVS_API ovvsStatus ovvsResourcesLastPhaseMs(ovvsResources_t res, float* ms, int32_t count);
 
+/* ---- kernel watchdog ---------------------------------------------------------------------- */
+
+/* Every wait inside this library's kernels (on a copy, an MMA, another warp or another GPU) is
+   bounded in time. A wait that runs out writes a watchdog code into the Resources' error word and
+   the kernel unwinds and returns, so the device context stays usable; the next synchronising call
+   on the Resources (a search, ovvsResourcesSynchronize) then returns OVVS_STATUS_ERROR. This call
+   writes the code that call saw (0 if none) and clears it. Codes: 0x101-0x109 waits of the fused
+   kernel (query tile, ring slot empty/full, TMEM buffer empty/full, query tile empty, unwinding,
+   side slot empty/full), 0x201 the self test below. Not in the reference. */
+OVVS_API ovvsStatus ovvsResourcesLastKernelError(ovvsResources_t res, int32_t* code);
+
+/* Runs a one-block kernel whose bounded wait is never satisfied, with a limit of `limit_ns`
+   nanoseconds (1e6..5e9), and checks that the watchdog fired: the kernel returns, the
+   synchronising call reports OVVS_STATUS_ERROR and the code is 0x201. Returns
+   OVVS_STATUS_SUCCESS and *code = 0x201 when that is what happened. Not in the reference. */
+OVVS_API ovvsStatus ovvsWatchdogSelfTest(ovvsResources_t res, int64_t limit_ns, int32_t* code);
+
 /* ---- device-pointer search ---------------------------------------------------------------- */
 
 /* Same contract as ovvsBruteForceSearch, but queries, bitset, neighbors and distances are device

@@ -90,6 +90,8 @@ def _bind(lib):
                                                c_void_p, c_void_p, c_void_p, c_void_p], c_int32),
         "ovvsResourcesSetProfiling": ([c_void_p, c_int32], c_int32),
         "ovvsResourcesLastPhaseMs": ([c_void_p, P(c_float), c_int32], c_int32),
+        "ovvsResourcesLastKernelError": ([c_void_p, P(c_int32)], c_int32),
+        "ovvsWatchdogSelfTest": ([c_void_p, c_int64, P(c_int32)], c_int32),
         "ovvsNcclUniqueIdSize": ([], c_int32),
         "ovvsNcclUniqueId": ([c_void_p, c_int32], c_int32),
         "ovvsResourcesCreateSharded": ([P(c_void_p), c_int32, c_int32, c_int32, c_void_p,
@@ -223,6 +225,18 @@ class Resources:
         ms = (c_float * 4)()
         _check(lib().ovvsResourcesLastPhaseMs(self._h, ms, 4), "phase times")
         return list(ms)
+
+    def last_kernel_error(self) -> int:
+        """Watchdog code seen by the last synchronising call that failed (0 if none); clears it."""
+        code = c_int32(0)
+        _check(lib().ovvsResourcesLastKernelError(self._h, byref(code)), "last kernel error")
+        return code.value
+
+    def watchdog_self_test(self, limit_ns: int = 50_000_000) -> int:
+        """Runs a kernel whose bounded wait is never satisfied; returns the watchdog code (0x201)."""
+        code = c_int32(0)
+        _check(lib().ovvsWatchdogSelfTest(self._h, int(limit_ns), byref(code)), "watchdog self test")
+        return code.value
 
 
 def nccl_unique_id() -> bytes:

@@ -718,16 +718,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFusedThreads, 1)
   if (warp == kEpiWarps) {
     if (lane == 0) run_producer(p, maps, s, lo, rank);
   } else if (warp == kEpiWarps + 1) {
-    if (lane == 0) {
-      if (rank == 0)
-        run_mma_dispatch(p, s, tmem_base, lo);
-      else  // the leader's MMAs read this CTA's shared memory and write its TMEM
-        drain_wait(s.drain, 0, p.err, s.abort);
-    }
+    if (lane == 0 && rank == 0) run_mma_dispatch(p, s, tmem_base, lo);
     __syncwarp();
   } else {
     run_epilogue<KL>(p, s, tmem_base, rank);
   }
+
+  // The leader's MMAs read the other CTA's shared memory and write its TMEM: that CTA waits for
+  // their completion (`drain`) before it may leave, but only once its own roles are done (its
+  // epilogue has consumed every tile), so the wait is short. Waiting from the start would span
+  // the whole launch and trip the watchdog on launches longer than its limit.
+  __syncthreads();
+  if (rank != 0 && warp == kEpiWarps + 1 && lane == 0) drain_wait(s.drain, 0, p.err, s.abort);
 
   // Neither CTA leaves (or frees TMEM) while the other may still arrive on its barriers.
   ptx::tc_fence_before();

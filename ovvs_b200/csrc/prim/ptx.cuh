@@ -59,13 +59,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // either this thread hit the time limit (it then records `code` in *err and raises *abort), or
 // another role of the CTA already raised *abort.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          int* err, int code) {
+                                          int* err, int code, uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > limit_ns) {
       atomicCAS(err, 0, code);
       *abort = 1;
       return false;

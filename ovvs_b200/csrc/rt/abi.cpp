@@ -13,6 +13,7 @@
 
 #include "../cluster/kmeans.hpp"
 #include "../neighbors/brute_force.hpp"
+#include "../prim/watchdog.cuh"
 #include "ovvs/ovvs.h"
 #include "ovvs/ovvs_cuda.h"
 #include "runtime.hpp"
@@ -458,6 +459,32 @@ ovvsStatus ovvsResourcesLastPhaseMs(ovvsResources_t res, float* ms, int32_t coun
     ms[i] = v;
   }
   return OVVS_STATUS_SUCCESS;
+}
+
+ovvsStatus ovvsResourcesLastKernelError(ovvsResources_t res, int32_t* code) {
+  if (!res || !code) return OVVS_STATUS_INVALID_ARGUMENT;
+  Resources& r = *from_handle(res);
+  std::lock_guard<std::mutex> lk(r.mu);
+  *code = r.last_kernel_error;
+  r.last_kernel_error = 0;
+  return OVVS_STATUS_SUCCESS;
+}
+
+ovvsStatus ovvsWatchdogSelfTest(ovvsResources_t res, int64_t limit_ns, int32_t* code) {
+  if (!res || !code || limit_ns < 1000000 || limit_ns > 5000000000LL)
+    return OVVS_STATUS_INVALID_ARGUMENT;
+  Resources& r = *from_handle(res);
+  std::lock_guard<std::mutex> lk(r.mu);
+  OVVS_TRY(r.check_policy());
+  OVVS_TRY(r.activate());
+  *code = 0;
+  OVVS_TRY_CUDA(ovvs::prim::launch_watchdog_selftest(r.d_err, static_cast<uint64_t>(limit_ns),
+                                                     r.stream));
+  const ovvsStatus st = r.finish();  // the wait ran out: ERROR, with the code recorded
+  *code = r.last_kernel_error;
+  r.last_kernel_error = 0;
+  if (st == OVVS_STATUS_ERROR && *code == ovvs::prim::kErrSelfTest) return OVVS_STATUS_SUCCESS;
+  return st == OVVS_STATUS_SUCCESS ? OVVS_STATUS_ERROR : st;
 }
 
 int32_t ovvsNcclUniqueIdSize(void) { return static_cast<int32_t>(sizeof(ncclUniqueId)); }

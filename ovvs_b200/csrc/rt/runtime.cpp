@@ -132,6 +132,7 @@ ovvsStatus Resources::finish() {
   int err = 0;
   OVVS_TRY_CUDA(cudaMemcpy(&err, d_err, sizeof(int), cudaMemcpyDeviceToHost));
   if (err != 0) {
+    last_kernel_error = err;
     cudaMemset(d_err, 0, sizeof(int));
     return OVVS_STATUS_ERROR;
   }

@@ -101,6 +101,7 @@ struct Resources {
   int world = 1;
   ncclComm_t comm = nullptr;
   int* d_err = nullptr;  // kernel watchdog word (device)
+  int last_kernel_error = 0;  // last nonzero watchdog code seen by finish()
   static constexpr int kPhases = 4;
   bool profiling = false;
   bool phase_valid = false;
