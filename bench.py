@@ -373,6 +373,8 @@ def run_ours(args, cfg):
     achieved = flops / (fused_ms / 1e3) / 1e12
     peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
     traffic = _traffic_from_profiles(args.config)
+    if traffic is not None:  # the profiled figure is for the whole config; a rank streams its shard
+        traffic *= (hi - lo) / n
     clk = clocks.summary()
 
     line = None
