@@ -48,7 +48,13 @@ CONFIGS = {
                 desc="L2 fp16, N=2M x 128 Gaussian mixture (1024 centres), Q=10k, k=10"),
     "c5": dict(metric="inner_product", dtype="f16", n=100_000_000, dim=96, nq=100_000, k=100,
                dist="unit", seed=4, desc="IP fp16, N=100M x 96 unit-norm, Q=100k, k=100"),
+    # k-means (ovvsKMeansFit): one step = one full fit of `iters` Lloyd iterations
+    "c4": dict(kind="kmeans", metric="l2", dtype="f32", n=5_000_000, dim=128, clusters=4096,
+               iters=10, dist="mixture", centres=4096, centre_std=3.0, seed=3,
+               desc="k-means fp32, N=5M x 128 Gaussian mixture (4096 centres, var 9), "
+                    "C=4096, 10 iterations"),
 }
+KMEANS_METRIC = "k-means Lloyd iterations/sec @ N=5M D=128 C=4096 fp32; % of roofline"
 METRIC_NAME = "kNN queries/sec @ N=10M D=128 fp16 k=10 at 1/2/4/8 B200; % of roofline"
 CHUNK = 1_000_000
 
@@ -228,9 +234,61 @@ def _reference_sizes(cfg, seconds):
     return threads, nq
 
 
+def _reference_kmeans_sample(cfg, data_host, rows):
+    """Times the reference's FORCE_CPU ovvsKMeansFit (its minimum of 4 iterations) on the first
+    `rows` rows with the config's cluster count. Returns (seconds, iterations)."""
+    from oracle.cpu import Reference
+
+    ref = Reference()
+    x = np.ascontiguousarray(data_host[:rows], np.float32)
+    t0 = time.perf_counter()
+    ref.kmeans(x, cfg["clusters"], 4, predict=False)
+    return time.perf_counter() - t0, 4
+
+
+def _reference_kmeans_rows(cfg, seconds):
+    rate = 2.1e9  # reference naive fp32 GEMM, FLOP/s on one thread (measured on C1)
+    rows = int(seconds * rate / (4 * 2.0 * cfg["clusters"] * cfg["dim"]))
+    return max(cfg["clusters"], min(cfg["n"], rows))
+
+
+def _reference_kmeans_line(args, cfg, secs, rows, iters):
+    # iterations/s of the full config, extrapolated linearly by rows (cost ~ N * C * D)
+    value = iters * len(secs) / sum(secs) * rows / cfg["n"]
+    sample = (f"{iters}-iteration fits of {rows} of {cfg['n']} rows x C={cfg['clusters']}, "
+              "FORCE_CPU (the reference fit is single-threaded), iterations/s scaled by "
+              f"{rows}/{cfg['n']} rows")
+    return value, sample
+
+
 def run_reference_arm(args, cfg):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
+        return 0
+    if cfg.get("kind") == "kmeans":
+        import torch
+
+        dev = "cuda" if torch.cuda.is_available() else "cpu"
+        rows = _reference_kmeans_rows(cfg, args.ref_seconds)
+        data_host = _gen_rows(cfg, 0, rows, dev, torch).cpu().numpy()
+        for _ in range(max(1, args.warmup // 3)):
+            _reference_kmeans_sample(cfg, data_host, min(rows, 2 * cfg["clusters"]))
+        runs = [_reference_kmeans_sample(cfg, data_host, rows) for _ in range(args.steps)]
+        secs = [r[0] for r in runs]
+        value, sample = _reference_kmeans_line(args, cfg, secs, rows, runs[0][1])
+        line = {
+            "metric": KMEANS_METRIC, "value": value, "unit": "iterations/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * sum(secs) / len(secs), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference", "config": {"workload": f"{args.config}: {cfg['desc']}",
+                                            "sample": sample},
+            "cpu_baseline": {"value": value, "unit": "iterations/s", "cores": 1,
+                             "kind": "reference", "sample": sample},
+            "e2e": {"value": value, "unit": "iterations/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
         return 0
     import torch
 
@@ -424,6 +482,132 @@ def run_ours(args, cfg):
     return 0
 
 
+def run_kmeans(args, cfg):
+    """k-means arm: each step is one ovvsKMeansFit (ovvsKMeansFitShard on N > 1 GPUs: rows
+    sharded, centroids replicated, fp64 sums all-reduced per iteration). `value` = Lloyd
+    iterations per second over the fit's device phase of iterations (CUDA events on the
+    library's stream, max over ranks); `e2e` = the same from the fit's wall time, which includes
+    the upload of the host dataset (pageable memory) and the centroid download."""
+    import torch
+    import torch.distributed as dist
+
+    import ovvs_b200 as ov
+    from ovvs_b200.shard import row_range
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+        uid = [ov.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        res = ov.Resources.sharded(local, rank, world, uid[0])
+    else:
+        res = ov.Resources.sharded(local, 0, 1, None)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    n, dim, C, iters = cfg["n"], cfg["dim"], cfg["clusters"], cfg["iters"]
+    lo, hi = row_range(rank, world, n)
+    shard = _gen_rows(cfg, lo, hi, dev, torch)
+    shard_host = np.ascontiguousarray(shard.cpu().numpy(), np.float32)
+    del shard
+    torch.cuda.synchronize()
+
+    def fit():
+        if world > 1:
+            return ov.KMeans(shard_host, nclusters=C, iters=iters, resources=res, row_offset=lo,
+                             n_total=n)
+        return ov.KMeans(shard_host, nclusters=C, iters=iters, resources=res)
+
+    res.set_profiling(True)
+    for _ in range(args.warmup):
+        fit().close()
+    barrier()
+    walls, iter_ms, up_ms = [], [], []
+    with ClockSampler(local) as clocks:
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            m = fit()
+            walls.append(time.perf_counter() - t0)
+            ph = res.last_phase_ms()
+            iter_ms.append(ph[1])
+            up_ms.append(ph[0])
+            m.close()
+        barrier()
+    res.set_profiling(False)
+    dev_s = max_over_ranks(sum(iter_ms) / 1e3)
+    wall_s = max_over_ranks(sum(walls))
+    total_iters = iters * args.steps
+    peaks, peak_kind = _peaks()
+    peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+    flops_local = 2.0 * (hi - lo) * C * dim * total_iters
+    achieved = flops_local / max_over_ranks(sum(iter_ms) / 1e3) / 1e12
+    clk = clocks.summary()
+    line = None
+    if rank == 0:
+        line = {
+            "metric": KMEANS_METRIC, "value": total_iters / dev_s, "unit": "iterations/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * dev_s / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{args.config}: {cfg['desc']}", "n": n, "dim": dim,
+                       "clusters": C, "iters": iters, "rows_per_gpu": hi - lo,
+                       "parallelism": ("1 GPU" if world == 1 else
+                                       f"rows sharded over {world} GPU(s), fp64 sums "
+                                       "all-reduced per iteration (NCCL)"),
+                       "l2": "inputs larger than L2 (dataset >> 126 MB), no flush needed",
+                       "upload_ms_mean": sum(up_ms) / len(up_ms),
+                       "fit_wall_s_mean": wall_s / args.steps},
+            "e2e": {"value": total_iters / wall_s, "unit": "iterations/s",
+                    "h2d_bytes_per_step": int(shard_host.nbytes),
+                    "d2h_bytes_per_step": int(C * dim * 4)},
+            # per iteration, ours: centroid index build (row stats, scatter, tile and group
+            # bounds), query prep, fused kernel, merge + re-rank, label keys, centroid update
+            "gpu_launches": 10 * total_iters,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                         "kernel": "knn_fused_kernel (assignment) + update",
+                         "flops_per_launch": 2.0 * (hi - lo) * C * dim,
+                         "note": "algorithmic 2*N*C*D per iteration; fp32 rows and points run "
+                                 "as three fp16 MMA passes (hi*hi + lo*hi + hi*lo)",
+                         "peak_source": f"{peak_kind} bf16 dense sustained (fp16 MMA rate)"},
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"],
+                       "reasons": clk["reasons"]},
+        }
+    if world > 1:
+        dist.barrier()
+    res.close()
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rows = _reference_kmeans_rows(cfg, args.ref_seconds)
+        secs, it = _reference_kmeans_sample(cfg, shard_host, rows)
+        value, sample = _reference_kmeans_line(args, cfg, [secs], rows, it)
+        line["cpu_baseline"] = {"value": value, "unit": "iterations/s", "cores": 1,
+                                "kind": "reference", "sample": sample}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -441,6 +625,8 @@ def main():
     cfg = CONFIGS[args.config]
     if args.impl == "reference":
         return run_reference_arm(args, cfg)
+    if cfg.get("kind") == "kmeans":
+        return run_kmeans(args, cfg)
     return run_ours(args, cfg)
 
 

@@ -7,6 +7,7 @@
 #include <algorithm>
 #include <random>
 
+#include "../prim/keys.cuh"
 #include "../prim/prep.cuh"
 
 namespace ovvs {
@@ -24,6 +25,40 @@ __global__ void label_keys_kernel(const int64_t* __restrict__ labels, int64_t n,
   keys[i] = c;
   idx[i] = static_cast<uint32_t>(i);
   atomicAdd(&counts[c], 1);
+}
+
+// Upper bound on each point's nearest-centroid ranking key for the next assignment: the point's
+// value against its previous centroid under the new centroids, v = |c|^2 - 2 x.c (the fused
+// kernel's L2 ranking value, without |x|^2), plus a relative margin of 1e-4 that covers the
+// rounding of this warp-parallel sum and of the kernel's own values. The true nearest centroid
+// has a value no larger, so seeding the kernel's shared bound with it filters from the first
+// tile without excluding it.
+__global__ void kmeans_bound_kernel(const float* __restrict__ x, const int64_t* __restrict__ labels,
+                                    const float* __restrict__ centroids, int dim, int64_t n,
+                                    uint64_t* __restrict__ bound) {
+  const int lane = threadIdx.x & 31;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (i >= n) return;
+  const int64_t lab = labels[i];
+  const float* xr = x + i * dim;
+  const float* cr = centroids + (lab < 0 ? 0 : lab) * dim;
+  float ip = 0.f, yn = 0.f;
+  for (int d = lane; d < dim; d += 32) {
+    const float c = cr[d];
+    ip = fmaf(xr[d], c, ip);
+    yn = fmaf(c, c, yn);
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) {
+    ip += __shfl_xor_sync(0xffffffffu, ip, off);
+    yn += __shfl_xor_sync(0xffffffffu, yn, off);
+  }
+  if (lane == 0) {
+    const float v = yn - 2.f * ip;
+    const float margin = 1e-4f * (fabsf(yn) + 2.f * fabsf(ip)) + 1e-30f;
+    const bool ok = lab >= 0 && v == v && fabsf(v) < __int_as_float(0x7f800000);
+    bound[i] = ok ? keys::make_key(v + margin, static_cast<uint32_t>(lab)) : keys::kEmptyKey;
+  }
 }
 
 // mixer.cpp:902-918: per centroid, fp32 sum of its rows in ascending row order, then
@@ -107,6 +142,8 @@ ovvsStatus fit(rt::Resources& r, const float* x, int64_t n_local, int64_t row_of
   const int32_t k = static_cast<int32_t>(std::max<int64_t>(1, std::min<int64_t>(nclusters, n_total)));
   m.k_eff = k;
   const size_t cbytes = static_cast<size_t>(k) * dim * sizeof(float);
+  // Profiling phases of a fit: [0] upload + seeding, [1] the Lloyd iterations, [2] download.
+  r.mark(0);
 
   // Seeding (mixer.cpp:880-890) over the global row numbering: each centroid row is copied by
   // the shard that owns it, the others contribute zeros, and a sum all-reduce assembles them.
@@ -131,6 +168,7 @@ ovvsStatus fit(rt::Resources& r, const float* x, int64_t n_local, int64_t row_of
 
   const int64_t n = n_local;
   OVVS_TRY_CUDA(m.labels.reserve(n * sizeof(int64_t) + 16));
+  OVVS_TRY_CUDA(m.bound_keys.reserve(n * sizeof(uint64_t) + 16));
   OVVS_TRY_CUDA(m.dist.reserve(n * sizeof(float) + 16));
   OVVS_TRY_CUDA(m.sort_keys.reserve(n * sizeof(uint32_t) + 16));
   OVVS_TRY_CUDA(m.sorted_keys.reserve(n * sizeof(uint32_t) + 16));
@@ -153,12 +191,26 @@ ovvsStatus fit(rt::Resources& r, const float* x, int64_t n_local, int64_t row_of
     OVVS_TRY_CUDA(m.cnt64.reserve(static_cast<size_t>(k) * sizeof(double)));
   }
 
+  r.mark(1);
+  r.mark_hold = true;
+  struct Release {
+    rt::Resources& r;
+    ~Release() { r.mark_hold = false; }
+  } release_marks{r};
   for (int32_t it = 0; it < iters; ++it) {
     OVVS_TRY(nb::build_from_device(r, m.index, m.d_centroids.get(), kDTypeF32, k, dim,
                                    OVVS_METRIC_L2_EXPANDED, 0));
     int64_t k_eff = 0;
+    // From the second iteration on, each point's previous centroid bounds its assignment.
+    if (it > 0 && n > 0) {
+      kmeans_bound_kernel<<<static_cast<unsigned>((n + 7) / 8), 256, 0, s>>>(
+          m.d_x.as<float>(), m.labels.as<int64_t>(), m.d_centroids.as<float>(),
+          static_cast<int>(dim), n, m.bound_keys.as<uint64_t>());
+      OVVS_TRY_CUDA(cudaGetLastError());
+    }
     OVVS_TRY(nb::search_device(r, m.index, m.d_x.as<float>(), n, 1, nullptr,
-                               m.labels.as<int64_t>(), m.dist.as<float>(), &k_eff));
+                               m.labels.as<int64_t>(), m.dist.as<float>(), &k_eff,
+                               it > 0 ? m.bound_keys.as<uint64_t>() : nullptr));
     OVVS_TRY_CUDA(cudaMemsetAsync(m.counts.get(), 0, static_cast<size_t>(k) * sizeof(int), s));
     if (n > 0) {
       label_keys_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(
@@ -198,10 +250,14 @@ ovvsStatus fit(rt::Resources& r, const float* x, int64_t n_local, int64_t row_of
       OVVS_TRY_CUDA(cudaGetLastError());
     }
   }
+  r.mark_hold = false;
+  r.mark(2);
   OVVS_TRY(nb::build_from_device(r, m.index, m.d_centroids.get(), kDTypeF32, k, dim,
                                  OVVS_METRIC_L2_EXPANDED, 0));
   m.host.assign(static_cast<size_t>(std::max(k, nclusters)) * dim, 0.f);
   OVVS_TRY_CUDA(cudaMemcpyAsync(m.host.data(), m.d_centroids.get(), cbytes, cudaMemcpyDeviceToHost, s));
+  r.mark(3);
+  r.mark(4);
   m.d_x.release();
   return r.finish();
 }

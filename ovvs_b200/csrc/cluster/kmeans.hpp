@@ -28,7 +28,7 @@ struct KMeansModel {
   nb::BruteIndex index;     // centroids as an L2 brute-force index (replicated)
   // iteration scratch
   rt::DeviceBuffer d_x, labels, dist, sort_keys, sorted_keys, idx, sorted_idx, counts, offsets,
-      cub_tmp, sum64, cnt64;
+      cub_tmp, sum64, cnt64, bound_keys;
 };
 
 // Rows [row_offset, row_offset + n_local) of a dataset with n_total rows (world == 1:

@@ -364,7 +364,7 @@ ovvsStatus search_large(rt::Resources& r, const BruteIndex& ix, const SearchCtx&
 
 ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_queries, int64_t nq,
                          int64_t k, const uint8_t* d_bitset, int64_t* d_neighbors,
-                         float* d_distances, int64_t* k_eff_out) {
+                         float* d_distances, int64_t* k_eff_out, const uint64_t* d_init_bound) {
   cudaStream_t s = r.stream;
   const int64_t k_eff = std::min<int64_t>(k, ix.n_total);
   *k_eff_out = k_eff;
@@ -436,6 +436,9 @@ ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_
     uint64_t* bound = nullptr;
     OVVS_TRY(r.scratch(rt::kWsBound, static_cast<size_t>(c.q_pad), &bound));
     OVVS_TRY_CUDA(cudaMemsetAsync(bound, 0xFF, static_cast<size_t>(c.q_pad) * sizeof(uint64_t), s));
+    if (d_init_bound)
+      OVVS_TRY_CUDA(cudaMemcpyAsync(bound, d_init_bound, static_cast<size_t>(nq) * sizeof(uint64_t),
+                                    cudaMemcpyDeviceToDevice, s));
     p.q_bound = bound;
     p.k_pub = static_cast<int>(k_eff);
     r.mark(1);

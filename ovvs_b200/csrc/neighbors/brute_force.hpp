@@ -53,9 +53,12 @@ ovvsStatus build_from_host(rt::Resources& r, BruteIndex& ix, const void* data, i
 
 // Enqueues a search on r.stream. d_queries [nq x dim] fp32, d_bitset null or global-id bitset,
 // outputs [nq x k_eff] with k_eff = min(k, n_total) (written to *k_eff_out).
+// d_init_bound (optional, small-k path): per-query key (keys.cuh) known to be >= the query's
+// k-th best ranking key (with margin); the fused kernel filters with it from its first tile.
 ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_queries, int64_t nq,
                          int64_t k, const uint8_t* d_bitset, int64_t* d_neighbors,
-                         float* d_distances, int64_t* k_eff_out);
+                         float* d_distances, int64_t* k_eff_out,
+                         const uint64_t* d_init_bound = nullptr);
 
 // Number of super-chunks per query tile for the fused kernel's work items (items = query tiles x
 // super-chunks), limited so the candidate lists stay under cand_per_sc_bytes * sc <= 1.5 GB.

@@ -77,8 +77,18 @@ __global__ void query_prep_kernel(const float* __restrict__ queries, int64_t nq,
   }
   if (__any_sync(0xffffffffu, any_lo) && lane == 0) atomicOr(lo_flag, 1);
   if (lane == 0) {
-    float s = 0.f;  // internal.hpp:221-225 nrm2sq, sequential
-    for (int d = 0; d < dim; ++d) s = __fadd_rn(s, __fmul_rn(x[d], x[d]));
+    // internal.hpp:221-225 nrm2sq: strictly sequential sum; loads batched 16 at a time so the
+    // lane waits for memory once per 16 elements.
+    float s = 0.f;
+    int d = 0;
+    for (; d + 16 <= dim; d += 16) {
+      float v[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = x[d + i];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) s = __fadd_rn(s, __fmul_rn(v[i], v[i]));
+    }
+    for (; d < dim; ++d) s = __fadd_rn(s, __fmul_rn(x[d], x[d]));
     xn[q] = s;
     const int rk = rank_kind_of(metric);
     const float sigma = hamming ? 1.f : pow2f(max(-149, -(e + e_db)));

@@ -45,18 +45,62 @@ __device__ __forceinline__ void list_insert(uint64_t (&L)[KL], uint64_t c) {
 //   other         sum (x-y)^2                  internal.hpp:269-270
 // Sums are sequential over d with separately rounded multiply and add, like the reference's
 // scalar loops; ip is cpu_gemm's sequential dot product (cpu_prims.cpp:48-58).
-__device__ float exact_rank(const MergeParams& p, const float* __restrict__ x, float xn,
-                            int64_t pos) {
+// The sums stay strictly sequential (the reference's order); only the loads are batched: 16
+// elements of each row are loaded before their 16 in-order multiply/adds, so a query pays one
+// memory latency per 16 dimensions instead of one per dimension.
+constexpr int kSeqBlock = 16;
+
+template <class Y>
+__device__ __forceinline__ float seq_dot(const float* __restrict__ x, Y y, int D) {
+  float ip = 0.f;
+  int d = 0;
+  for (; d + kSeqBlock <= D; d += kSeqBlock) {
+    float xv[kSeqBlock], yv[kSeqBlock];
+#pragma unroll
+    for (int i = 0; i < kSeqBlock; ++i) {
+      xv[i] = x[d + i];
+      yv[i] = y(d + i);
+    }
+#pragma unroll
+    for (int i = 0; i < kSeqBlock; ++i) ip = __fadd_rn(ip, __fmul_rn(xv[i], yv[i]));
+  }
+  for (; d < D; ++d) ip = __fadd_rn(ip, __fmul_rn(x[d], y(d)));
+  return ip;
+}
+
+template <class Y>
+__device__ __forceinline__ float seq_sqdiff(const float* __restrict__ x, Y y, int D) {
+  float s = 0.f;
+  int d = 0;
+  for (; d + kSeqBlock <= D; d += kSeqBlock) {
+    float xv[kSeqBlock], yv[kSeqBlock];
+#pragma unroll
+    for (int i = 0; i < kSeqBlock; ++i) {
+      xv[i] = x[d + i];
+      yv[i] = y(d + i);
+    }
+#pragma unroll
+    for (int i = 0; i < kSeqBlock; ++i) {
+      const float t = __fsub_rn(xv[i], yv[i]);
+      s = __fadd_rn(s, __fmul_rn(t, t));
+    }
+  }
+  for (; d < D; ++d) {
+    const float t = __fsub_rn(x[d], y(d));
+    s = __fadd_rn(s, __fmul_rn(t, t));
+  }
+  return s;
+}
+
+template <class Y>
+__device__ __forceinline__ float exact_rank_with(const MergeParams& p, const float* __restrict__ x,
+                                                 float xn, int64_t pos, Y y_at) {
   const int D = p.dim;
-  const float* y32 = p.exact32 ? p.exact32 + pos * D : nullptr;
-  const __half* y16 = p.rows16 + pos * p.rows16_stride;
-  auto y_at = [&](int d) -> float { return y32 ? y32[d] : __half2float(y16[d]); };
   switch (p.metric) {
     case kMetricL2:
     case kMetricInnerProduct:
     case kMetricCosine: {
-      float ip = 0.f;
-      for (int d = 0; d < D; ++d) ip = __fadd_rn(ip, __fmul_rn(x[d], y_at(d)));
+      const float ip = seq_dot(x, y_at, D);
       if (p.metric == kMetricInnerProduct) return -ip;
       const float yn = p.norm_sorted[pos];
       if (p.metric == kMetricL2) return __fsub_rn(__fadd_rn(xn, yn), __fmul_rn(2.f, ip));
@@ -70,15 +114,23 @@ __device__ float exact_rank(const MergeParams& p, const float* __restrict__ x, f
       return static_cast<float>(c);
     }
     default: {
-      float s = 0.f;
-      for (int d = 0; d < D; ++d) {
-        const float t = __fsub_rn(x[d], y_at(d));
-        s = __fadd_rn(s, __fmul_rn(t, t));
-      }
+      const float s = seq_sqdiff(x, y_at, D);
       if (p.metric == kMetricL2Sqrt || p.metric == kMetricLp) return __fsqrt_rn(s);
       return s;
     }
   }
+}
+
+// Sums are sequential over d with separately rounded multiply and add, like the reference's
+// scalar loops; ip is cpu_gemm's sequential dot product (cpu_prims.cpp:48-58).
+__device__ float exact_rank(const MergeParams& p, const float* __restrict__ x, float xn,
+                            int64_t pos) {
+  if (p.exact32) {
+    const float* __restrict__ y32 = p.exact32 + pos * p.dim;
+    return exact_rank_with(p, x, xn, pos, [&](int d) { return y32[d]; });
+  }
+  const __half* __restrict__ y16 = p.rows16 + pos * p.rows16_stride;
+  return exact_rank_with(p, x, xn, pos, [&](int d) { return __half2float(y16[d]); });
 }
 
 template <int KL>

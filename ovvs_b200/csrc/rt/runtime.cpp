@@ -100,7 +100,7 @@ Resources::~Resources() {
 }
 
 void Resources::mark(int i) {
-  if (!profiling) return;
+  if (!profiling || mark_hold) return;
   if (!phase_ev[i] && cudaEventCreate(&phase_ev[i]) != cudaSuccess) {
     (void)cudaGetLastError();
     return;

@@ -117,8 +117,10 @@ struct Resources {
   ovvsStatus check_policy() const;
   // Waits for the stream, then reads and clears the watchdog word.
   ovvsStatus finish();
-  // Records phase boundary `i` (0..kPhases) of the current search when profiling.
+  // Records phase boundary `i` (0..kPhases) of the current search when profiling (ignored while
+  // mark_hold is set: a k-means fit keeps its own phases while its searches run).
   void mark(int i);
+  bool mark_hold = false;
   template <class T>
   ovvsStatus scratch(WorkSlot slot, size_t count, T** out) {
     const cudaError_t e = ws[slot].reserve(count * sizeof(T) + 16);
