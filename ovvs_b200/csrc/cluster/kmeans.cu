@@ -208,9 +208,12 @@ ovvsStatus fit(rt::Resources& r, const float* x, int64_t n_local, int64_t row_of
           static_cast<int>(dim), n, m.bound_keys.as<uint64_t>());
       OVVS_TRY_CUDA(cudaGetLastError());
     }
+    // The points' query operands (fp16 split, norms) are the same every iteration.
+    if (it == 0 && n > 0) OVVS_TRY(nb::prepare_queries(r, m.index, m.d_x.as<float>(), n, m.prepared));
     OVVS_TRY(nb::search_device(r, m.index, m.d_x.as<float>(), n, 1, nullptr,
                                m.labels.as<int64_t>(), m.dist.as<float>(), &k_eff,
-                               it > 0 ? m.bound_keys.as<uint64_t>() : nullptr));
+                               it > 0 ? m.bound_keys.as<uint64_t>() : nullptr, &m.prepared,
+                               /*labels_only=*/true));
     OVVS_TRY_CUDA(cudaMemsetAsync(m.counts.get(), 0, static_cast<size_t>(k) * sizeof(int), s));
     if (n > 0) {
       label_keys_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(
@@ -252,6 +255,11 @@ ovvsStatus fit(rt::Resources& r, const float* x, int64_t n_local, int64_t row_of
   }
   r.mark_hold = false;
   r.mark(2);
+  // free the per-fit query operands
+  m.prepared.a16.release();
+  m.prepared.xn.release();
+  m.prepared.e_q.release();
+  m.prepared.nq = 0;
   OVVS_TRY(nb::build_from_device(r, m.index, m.d_centroids.get(), kDTypeF32, k, dim,
                                  OVVS_METRIC_L2_EXPANDED, 0));
   m.host.assign(static_cast<size_t>(std::max(k, nclusters)) * dim, 0.f);

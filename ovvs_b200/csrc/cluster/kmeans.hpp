@@ -29,6 +29,7 @@ struct KMeansModel {
   // iteration scratch
   rt::DeviceBuffer d_x, labels, dist, sort_keys, sorted_keys, idx, sorted_idx, counts, offsets,
       cub_tmp, sum64, cnt64, bound_keys;
+  nb::PreparedQueries prepared;  // the points as query operands, during a fit
 };
 
 // Rows [row_offset, row_offset + n_local) of a dataset with n_total rows (world == 1:

@@ -362,9 +362,31 @@ ovvsStatus search_large(rt::Resources& r, const BruteIndex& ix, const SearchCtx&
 
 }  // namespace
 
+ovvsStatus prepare_queries(rt::Resources& r, const BruteIndex& ix, const float* d_queries,
+                           int64_t nq, PreparedQueries& pq) {
+  cudaStream_t s = r.stream;
+  pq.nq = nq;
+  pq.q_pad = prim::pad_queries(nq);
+  pq.dp = ix.dp;
+  pq.metric = ix.metric;
+  OVVS_TRY_CUDA(pq.a16.reserve(static_cast<size_t>(pq.q_pad) * 2 * ix.dp * sizeof(__half)));
+  OVVS_TRY_CUDA(pq.xn.reserve(static_cast<size_t>(pq.q_pad) * sizeof(float)));
+  OVVS_TRY_CUDA(pq.e_q.reserve(static_cast<size_t>(pq.q_pad) * sizeof(int16_t)));
+  OVVS_TRY_CUDA(pq.flag.reserve(sizeof(int)));
+  float* q_mul = nullptr;
+  OVVS_TRY(r.scratch(rt::kWsQueryMul, pq.q_pad, &q_mul));
+  OVVS_TRY_CUDA(cudaMemsetAsync(pq.flag.get(), 0, sizeof(int), s));
+  prim::launch_query_prep(d_queries, nq, pq.q_pad, static_cast<int>(ix.dim), ix.dp, ix.metric,
+                          ix.e_db, pq.a16.as<__half>(), q_mul, pq.xn.as<float>(),
+                          pq.flag.as<int>(), s, pq.e_q.as<int16_t>());
+  OVVS_TRY_CUDA(cudaGetLastError());
+  return OVVS_STATUS_SUCCESS;
+}
+
 ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_queries, int64_t nq,
                          int64_t k, const uint8_t* d_bitset, int64_t* d_neighbors,
-                         float* d_distances, int64_t* k_eff_out, const uint64_t* d_init_bound) {
+                         float* d_distances, int64_t* k_eff_out, const uint64_t* d_init_bound,
+                         const PreparedQueries* prepared, bool labels_only) {
   cudaStream_t s = r.stream;
   const int64_t k_eff = std::min<int64_t>(k, ix.n_total);
   *k_eff_out = k_eff;
@@ -376,13 +398,23 @@ ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_
   c.q_pad = prim::pad_queries(nq);
   c.num_qtiles = static_cast<int>(c.q_pad / kTileQ);
   r.mark(0);
-  OVVS_TRY(r.scratch(rt::kWsQueryA, static_cast<size_t>(c.q_pad) * 2 * ix.dp, &c.a16));
   OVVS_TRY(r.scratch(rt::kWsQueryMul, c.q_pad, &c.q_mul));
-  OVVS_TRY(r.scratch(rt::kWsQueryNorm, c.q_pad, &c.xn));
-  OVVS_TRY(r.scratch(rt::kWsFlags, 4, &c.flag));
-  OVVS_TRY_CUDA(cudaMemsetAsync(c.flag, 0, sizeof(int), s));
-  prim::launch_query_prep(d_queries, nq, c.q_pad, dim, ix.dp, ix.metric, ix.e_db, c.a16, c.q_mul,
-                          c.xn, c.flag, s);
+  const bool reuse = prepared && prepared->nq == nq && prepared->q_pad == c.q_pad &&
+                     prepared->dp == ix.dp && prepared->metric == ix.metric;
+  if (reuse) {
+    c.a16 = prepared->a16.as<__half>();
+    c.xn = prepared->xn.as<float>();
+    c.flag = prepared->flag.as<int>();
+    prim::launch_query_mul(prepared->e_q.as<int16_t>(), nq, c.q_pad, ix.metric, ix.e_db,
+                           c.q_mul, s);
+  } else {
+    OVVS_TRY(r.scratch(rt::kWsQueryA, static_cast<size_t>(c.q_pad) * 2 * ix.dp, &c.a16));
+    OVVS_TRY(r.scratch(rt::kWsQueryNorm, c.q_pad, &c.xn));
+    OVVS_TRY(r.scratch(rt::kWsFlags, 4, &c.flag));
+    OVVS_TRY_CUDA(cudaMemsetAsync(c.flag, 0, sizeof(int), s));
+    prim::launch_query_prep(d_queries, nq, c.q_pad, dim, ix.dp, ix.metric, ix.e_db, c.a16,
+                            c.q_mul, c.xn, c.flag, s);
+  }
   OVVS_TRY_CUDA(cudaGetLastError());
   if (d_bitset) {
     OVVS_TRY(r.scratch(rt::kWsAllow, ix.n_pad / 32, &c.allow));
@@ -401,6 +433,7 @@ ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_
   c.maps.b16 = ix.b16;
 
   prim::MergeParams m = merge_params(ix, c, d_queries, nq, k_eff);
+  m.labels_only = labels_only && r.world <= 1 ? 1 : 0;
   float *srank = nullptr, *grank = nullptr;
   int64_t *sgid = nullptr, *ggid = nullptr;
   const size_t cnt = static_cast<size_t>(nq) * k_eff;

@@ -51,6 +51,19 @@ ovvsStatus build_from_host(rt::Resources& r, BruteIndex& ix, const void* data, i
                            int64_t n, int64_t dim, int metric_raw, int64_t row_offset,
                            bool sharded);
 
+// Query operands prepared once for repeated searches of the same queries against indexes of the
+// same padded dim and metric (a k-means fit searches the same points every Lloyd iteration): the
+// scaled fp16 hi | lo rows, the reference-order norms, the lo-pass flag and each query's scale
+// exponent. Only the per-query multiplier depends on the index (its exponent) and is recomputed
+// per search.
+struct PreparedQueries {
+  int64_t nq = 0, q_pad = 0;
+  int dp = 0, metric = -1;
+  rt::DeviceBuffer a16, xn, e_q, flag;
+};
+ovvsStatus prepare_queries(rt::Resources& r, const BruteIndex& ix, const float* d_queries,
+                           int64_t nq, PreparedQueries& pq);
+
 // Enqueues a search on r.stream. d_queries [nq x dim] fp32, d_bitset null or global-id bitset,
 // outputs [nq x k_eff] with k_eff = min(k, n_total) (written to *k_eff_out).
 // d_init_bound (optional, small-k path): per-query key (keys.cuh) known to be >= the query's
@@ -58,7 +71,8 @@ ovvsStatus build_from_host(rt::Resources& r, BruteIndex& ix, const void* data, i
 ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_queries, int64_t nq,
                          int64_t k, const uint8_t* d_bitset, int64_t* d_neighbors,
                          float* d_distances, int64_t* k_eff_out,
-                         const uint64_t* d_init_bound = nullptr);
+                         const uint64_t* d_init_bound = nullptr,
+                         const PreparedQueries* prepared = nullptr, bool labels_only = false);
 
 // Number of super-chunks per query tile for the fused kernel's work items (items = query tiles x
 // super-chunks), limited so the candidate lists stay under cand_per_sc_bytes * sc <= 1.5 GB.

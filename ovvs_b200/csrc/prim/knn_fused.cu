@@ -529,6 +529,51 @@ __device__ __forceinline__ void slow_path(const FusedParams& p, const float (&r)
 }
 
 
+// The exact path for a deferred chunk: `row` = this lane's 32 values in shared memory and
+// row[32] = the bits of the columns that passed the threshold when it was saved (a superset of
+// those that pass now: thresholds only tighten). Only those columns are read back.
+template <int KL>
+__device__ __forceinline__ void check_row(const FusedParams& p, const float* row, int64_t col0,
+                                          int ct0, const uint8_t* side, EpiState<KL>& st) {
+  const float* aux = reinterpret_cast<const float*>(side + kSideAuxOff);
+  const uint32_t* ids = reinterpret_cast<const uint32_t*>(side + kSideIdOff);
+  const uint32_t* allow = reinterpret_cast<const uint32_t*>(side + kSideAllowOff);
+  uint32_t mask = __float_as_uint(row[32]);
+  while (mask) {
+    const int j = __ffs(mask) - 1;
+    mask &= mask - 1;
+    const float sv = row[j];
+    if (sv < st.thr) continue;  // threshold tightened by an earlier insertion
+    const int64_t pos = col0 + j;
+    if (pos >= p.n_rows) break;
+    float v;
+    const int ct = ct0 + j;
+    const bool allowed = p.allow == nullptr || ((allow[ct >> 5] >> (ct & 31)) & 1u);
+    if (!allowed) {
+      v = kInf;
+    } else if (p.rank_kind == kRankAffine) {
+      v = fmaf(sv, st.m, aux[ct]);
+    } else if (p.rank_kind == kRankScaled) {
+      v = sv * st.m;
+    } else {
+      v = sv * aux[ct];
+    }
+    const uint64_t key = keys::make_key(v, ids[ct]);
+    if constexpr (KL == 0) {
+      if (st.by_key ? key <= st.gkey : v <= st.gw) {
+        const uint32_t slot = atomicAdd(p.app_count + st.qi, 1u);
+        if (slot < static_cast<uint32_t>(p.app_cap))
+          p.app_buf[static_cast<size_t>(st.qi) * p.app_cap + slot] = key;
+      }
+    } else {
+      if (key < st.L[KL - 1]) {
+        list_insert<KL>(st.L, key);
+        refresh_threshold<KL>(st, p.rank_kind);
+      }
+    }
+  }
+}
+
 template <int KL>
 __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_base, uint32_t rank) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -629,8 +674,13 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
         ptx::tmem_wait_ld();
         if (!(max32(r0) < st.thr)) {
           if (saved < 0) {
+            uint32_t cand = 0;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) my_row[j] = r0[j];
+            for (int j = 0; j < 32; ++j) {
+              my_row[j] = r0[j];
+              cand |= static_cast<uint32_t>(!(r0[j] < st.thr)) << j;
+            }
+            my_row[32] = __uint_as_float(cand);
             saved = c;
           } else {
             flagged |= 1u << c;
@@ -652,12 +702,7 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive_cluster(tempty_l + buf * 8);
-      if (saved >= 0) {
-        float r0[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) r0[j] = my_row[j];
-        slow_path<KL>(p, r0, col0 + 32 * saved, ct0 + 32 * saved, side, st);
-      }
+      if (saved >= 0) check_row<KL>(p, my_row, col0 + 32 * saved, ct0 + 32 * saved, side, st);
       // Side slot released once this warp's exact checks of the tile are done.
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&s.side_empty[sb]);

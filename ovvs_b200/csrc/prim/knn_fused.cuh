@@ -64,7 +64,7 @@ constexpr int kSideAuxOff = 0;             // side slot: aux[256] fp32
 constexpr int kSideIdOff = 1024;           //            row id[256] u32
 constexpr int kSideAllowOff = 2048;        //            allow bits[256] (8 words)
 constexpr int kSideBytes = 2176;           // slot stride (multiple of 128 bytes)
-constexpr int kDeferStride = 33;           // floats per deferred row (32 values + chunk index;
+constexpr int kDeferStride = 33;           // floats per deferred row (32 values + candidate mask;
                                            // 33 keeps the lanes' rows on distinct banks)
 
 enum RankKind : int { kRankAffine = 0, kRankScaled = 1, kRankColumnScaled = 2 };

@@ -25,10 +25,16 @@ __device__ __forceinline__ float pow2f(int e) {
   return __int_as_float(1 << (e + 149));
 }
 
+__device__ __forceinline__ float query_mul(int metric, int e, int e_db) {
+  const int rk = rank_kind_of(metric);
+  const float sigma = metric == kMetricHamming ? 1.f : pow2f(max(-149, -(e + e_db)));
+  return rk == kRankAffine ? -2.f * sigma : (rk == kRankScaled ? -sigma : 1.f);
+}
+
 __global__ void query_prep_kernel(const float* __restrict__ queries, int64_t nq, int64_t q_pad,
                                   int dim, int dp, int metric, int e_db, __half* __restrict__ a16,
                                   float* __restrict__ q_mul, float* __restrict__ xn,
-                                  int* __restrict__ lo_flag) {
+                                  int* __restrict__ lo_flag, int16_t* __restrict__ e_out) {
   const int lane = threadIdx.x & 31;
   const int64_t q = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (q >= q_pad) return;
@@ -43,6 +49,7 @@ __global__ void query_prep_kernel(const float* __restrict__ queries, int64_t nq,
     if (lane == 0) {
       q_mul[q] = -1.f;
       xn[q] = 0.f;
+      if (e_out) e_out[q] = 0;
     }
     return;
   }
@@ -90,9 +97,8 @@ __global__ void query_prep_kernel(const float* __restrict__ queries, int64_t nq,
     }
     for (; d < dim; ++d) s = __fadd_rn(s, __fmul_rn(x[d], x[d]));
     xn[q] = s;
-    const int rk = rank_kind_of(metric);
-    const float sigma = hamming ? 1.f : pow2f(max(-149, -(e + e_db)));
-    q_mul[q] = rk == kRankAffine ? -2.f * sigma : (rk == kRankScaled ? -sigma : 1.f);
+    q_mul[q] = query_mul(metric, e, e_db);
+    if (e_out) e_out[q] = static_cast<int16_t>(e);
   }
 }
 
@@ -232,11 +238,26 @@ __global__ void allow_bits_kernel(const uint8_t* __restrict__ bitset, int64_t ro
 
 void launch_query_prep(const float* queries, int64_t nq, int64_t q_pad, int dim, int dp,
                        int metric_code, int e_db, __half* a16, float* q_mul, float* xn,
-                       int* lo_flag, cudaStream_t stream) {
+                       int* lo_flag, cudaStream_t stream, int16_t* e_q) {
   const int wpb = 8;
   const int64_t blocks = (q_pad + wpb - 1) / wpb;
   query_prep_kernel<<<static_cast<unsigned>(blocks), wpb * 32, 0, stream>>>(
-      queries, nq, q_pad, dim, dp, metric_code, e_db, a16, q_mul, xn, lo_flag);
+      queries, nq, q_pad, dim, dp, metric_code, e_db, a16, q_mul, xn, lo_flag, e_q);
+}
+
+namespace {
+__global__ void query_mul_kernel(const int16_t* __restrict__ e_q, int64_t nq, int64_t q_pad,
+                                 int metric, int e_db, float* __restrict__ q_mul) {
+  const int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (q >= q_pad) return;
+  q_mul[q] = q < nq ? query_mul(metric, e_q[q], e_db) : -1.f;
+}
+}  // namespace
+
+void launch_query_mul(const int16_t* e_q, int64_t nq, int64_t q_pad, int metric_code, int e_db,
+                      float* q_mul, cudaStream_t stream) {
+  query_mul_kernel<<<static_cast<unsigned>((q_pad + 255) / 256), 256, 0, stream>>>(
+      e_q, nq, q_pad, metric_code, e_db, q_mul);
 }
 
 void launch_row_stats(const void* data, int dtype, int64_t n, int dim, int metric_code,

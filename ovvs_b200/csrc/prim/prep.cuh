@@ -45,7 +45,12 @@ inline int normalize_metric(int m) { return (m >= 0 && m <= 5) ? m : kMetricDire
 // *lo_flag = 1 if any lo element is non-zero. e_db is the database's power-of-two scale.
 void launch_query_prep(const float* queries, int64_t nq, int64_t q_pad, int dim, int dp,
                        int metric_code, int e_db, __half* a16, float* q_mul, float* xn,
-                       int* lo_flag, cudaStream_t stream);
+                       int* lo_flag, cudaStream_t stream, int16_t* e_q = nullptr);
+
+// q_mul from the per-query exponents a previous launch_query_prep wrote to e_q, for an index
+// with exponent e_db (what query prep computes, without re-reading the queries).
+void launch_query_mul(const int16_t* e_q, int64_t nq, int64_t q_pad, int metric_code, int e_db,
+                      float* q_mul, cudaStream_t stream);
 
 // Per-row statistics of the database in original order. data: raw [n x dim] of `dtype`
 // (ovvsDType). Writes norm[n] (sequential fp32 squared norm of the decoded row), sort_key[n]

@@ -140,36 +140,79 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t q = static_cast<int64_t>(blockIdx.x) * kMergeWarps + warp;
   if (q >= p.nq) return;
-  uint64_t* lists = merge_smem + warp * 32 * KL;
-
-  // 1. Each lane keeps the KL best keys of a strided share of the candidates.
-  uint64_t L[KL];
-#pragma unroll
-  for (int i = 0; i < KL; ++i) L[i] = kEmptyKey;
   const uint64_t* c = p.cand + static_cast<size_t>(q) * p.num_sc * KL;
   const int total = p.num_sc * KL;
-  for (int e = lane; e < total; e += 32) {
-    const uint64_t key = c[e];
-    if (key < L[KL - 1]) list_insert<KL>(L, key);
-  }
-#pragma unroll
-  for (int i = 0; i < KL; ++i) lists[lane * KL + i] = L[i];
-  __syncwarp();
-
-  // 2. Merge the 32 sorted lane lists: lane r receives the r-th best key overall.
-  int ptr = 0;
   uint64_t sel = kEmptyKey;
-  for (int r = 0; r < KL; ++r) {
-    uint64_t k = ptr < KL ? lists[lane * KL + ptr] : kEmptyKey;
-    int l = lane;
-    warp_argmin(k, l);
-    if (lane == l) ++ptr;
-    if (lane == r) sel = k;
+  if (total <= 32) {
+    // Few candidates (small k, few lists, e.g. a k-means assignment): one per lane, a 32-key
+    // bitonic sort, lane r keeps the r-th best.
+    uint64_t key = lane < total ? c[lane] : kEmptyKey;
+#pragma unroll
+    for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        const uint64_t other = __shfl_xor_sync(kFull, key, stride);
+        const bool up = (lane & size) == 0;
+        const bool lower = (lane & stride) == 0;
+        const bool take_min = lower == up;
+        key = take_min ? (other < key ? other : key) : (other > key ? other : key);
+      }
+    }
+    sel = lane < KL ? key : kEmptyKey;
+  } else {
+    uint64_t* lists = merge_smem + warp * 32 * KL;
+    // 1. Each lane keeps the KL best keys of a strided share of the candidates.
+    uint64_t L[KL];
+#pragma unroll
+    for (int i = 0; i < KL; ++i) L[i] = kEmptyKey;
+    for (int e = lane; e < total; e += 32) {
+      const uint64_t key = c[e];
+      if (key < L[KL - 1]) list_insert<KL>(L, key);
+    }
+#pragma unroll
+    for (int i = 0; i < KL; ++i) lists[lane * KL + i] = L[i];
+    __syncwarp();
+
+    // 2. Merge the 32 sorted lane lists: lane r receives the r-th best key overall.
+    int ptr = 0;
+    for (int r = 0; r < KL; ++r) {
+      uint64_t k = ptr < KL ? lists[lane * KL + ptr] : kEmptyKey;
+      int l = lane;
+      warp_argmin(k, l);
+      if (lane == l) ++ptr;
+      if (lane == r) sel = k;
+    }
   }
 
   // 3. Exact distance of each survivor.
   const float* x = p.queries + q * p.dim;
   const float xn = p.xn[q];
+  if (p.labels_only && p.k_eff == 1 && p.neighbors && p.allow == nullptr &&
+      p.metric == kMetricL2) {
+    // The approximate ranking values v = |y|^2 - 2 x.y differ from the exact ones by at most
+    // ~1e-6 (|x| |y| + |v|) (split fp16 products, fp32 sums); with a 10x wider margin, a best
+    // candidate that beats the second by more than it is the exact argmin, ties included.
+    const uint64_t k0 = __shfl_sync(kFull, sel, 0), k1 = __shfl_sync(kFull, sel, 1);
+    if (k0 != kEmptyKey) {
+      const float v0 = keys::key_value(k0);
+      const float v1 = k1 == kEmptyKey ? __int_as_float(0x7f800000) : keys::key_value(k1);
+      const float yn0 = p.norm_sorted[p.inv_perm[keys::key_id(k0)]];
+      const float yn1 = k1 == kEmptyKey ? 0.f : p.norm_sorted[p.inv_perm[keys::key_id(k1)]];
+      const float fin = __int_as_float(0x7f800000);
+      const bool finite = fabsf(v0) < fin && fabsf(xn) < fin && fabsf(yn0) < fin &&
+                          fabsf(yn1) < fin && !(v1 != v1);
+      const float margin =
+          1e-5f * (fabsf(v0) + (k1 == kEmptyKey ? 0.f : fabsf(v1)) + xn + yn0 + yn1 +
+                   2.f * sqrtf(xn * yn0) + 2.f * sqrtf(xn * yn1)) + 1e-30f;
+      if (finite && v1 - v0 > margin) {
+        if (lane == 0) {
+          p.neighbors[q] = p.row_offset + static_cast<int64_t>(keys::key_id(k0));
+          p.distances[q] = __fadd_rn(xn, v0);
+        }
+        return;
+      }
+    }
+  }
   float rank = __int_as_float(0x7fffffff);
   uint64_t key = kEmptyKey;
   if (sel != kEmptyKey) {

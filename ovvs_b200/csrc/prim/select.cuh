@@ -39,6 +39,10 @@ struct MergeParams {
   float* shard_rank;         // [nq][k_eff] or null
   int64_t* shard_gid;
   int negate_output;         // inner product: report -rank (= +dot)
+  // k-means assignment (one GPU, L2, k = 1, no bitset): when the best candidate's approximate
+  // value is below the second's by more than their error bound, its id is the exact argmin and
+  // is written without the exact recomputation (the distance written is then approximate).
+  int labels_only;
 };
 
 cudaError_t launch_merge_rerank(const MergeParams& p, cudaStream_t stream);
