@@ -29,7 +29,10 @@ size_t elem_size(int dtype) {
 }
 
 // Splits dp (multiple of 16) into K chunks of 64 (SWIZZLE_128B), then 32 / 16 for the tail.
-void plan_chunks(int dp, int* nchunk, int* cx, int* cw) {
+// Splits a padded dim into K chunks of 64 fp16 columns plus 32- and 16-wide tails. Returns false
+// (writing nothing past `cap`) when more than `cap` chunks would be needed.
+bool plan_chunks(int dp, int cap, int* nchunk, int* cx, int* cw) {
+  if (dp / 64 + 2 > cap) return false;
   int n = 0, x = 0;
   while (dp - x >= 64) {
     cx[n] = x;
@@ -47,6 +50,7 @@ void plan_chunks(int dp, int* nchunk, int* cx, int* cw) {
     x += 16;
   }
   *nchunk = n;
+  return true;
 }
 
 }  // namespace
@@ -98,8 +102,8 @@ ovvsStatus build_from_device(rt::Resources& r, BruteIndex& ix, const void* d_dat
   ix.metric = prim::normalize_metric(metric_raw);
   ix.dtype = dtype;
   ix.dp = static_cast<int>((dim + 15) / 16 * 16);
-  plan_chunks(ix.dp, &ix.nchunk, ix.chunk_x, ix.chunk_w);
-  if (ix.nchunk > prim::kMaxChunks) return OVVS_STATUS_UNSUPPORTED;
+  if (!plan_chunks(ix.dp, prim::kMaxChunks, &ix.nchunk, ix.chunk_x, ix.chunk_w))
+    return OVVS_STATUS_UNSUPPORTED;
   const bool hamming = ix.metric == prim::kMetricHamming;
   ix.b_parts = (dtype == kDTypeF32 && !hamming) ? 2 : 1;
   ix.n_pad = (n + kTileN - 1) / kTileN * kTileN;

@@ -100,6 +100,23 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* 
 // ------------------------------------------------------------------------------------------
 // TMA producer (one thread)
 // ------------------------------------------------------------------------------------------
+// Per tile: the 256 rows' aux values, ids and allow bits into side slot tile % kSideBufs, once
+// the epilogue has released it. Returns false when the wait gave up.
+__device__ __forceinline__ bool load_side(const FusedParams& p, const Smem& s, int t,
+                                          uint32_t tile, bool need_aux, uint32_t side_tx) {
+  const uint32_t sb = tile % kSideBufs, suse = tile / kSideBufs;
+  if (suse > 0 && !ptx::mbar_wait(&s.side_empty[sb], (suse - 1) & 1, s.abort, p.err,
+                                  kErrWaitSideEmpty))
+    return false;
+  const int64_t pos0 = static_cast<int64_t>(t) * p.tile_stride * kTileN;
+  uint8_t* slot_side = s.side + sb * kSideBytes;
+  ptx::mbar_arrive_expect_tx(&s.side_full[sb], side_tx);
+  if (need_aux) ptx::bulk_load(slot_side + kSideAuxOff, p.row_aux + pos0, 1024, &s.side_full[sb]);
+  ptx::bulk_load(slot_side + kSideIdOff, p.row_id + pos0, 1024, &s.side_full[sb]);
+  if (p.allow) ptx::bulk_load(slot_side + kSideAllowOff, p.allow + pos0 / 32, 32, &s.side_full[sb]);
+  return true;
+}
+
 // Both CTAs of the pair run a producer: each loads its own 128 queries and its own 128-row half
 // of every database chunk into its own shared memory. The copies are counted on the leader's
 // full / afull barriers (the leader arms them with the bytes of both CTAs); each producer learns
@@ -141,18 +158,10 @@ __device__ void run_producer(const FusedParams& p, const FusedMaps& maps, const 
     }
     for (int t = it.t0; t < it.t1 && ok; ++t) {
       // Side data first: the epilogue needs it only after this tile's MMAs.
-      const uint32_t sb = tile % kSideBufs, suse = tile / kSideBufs;
-      if (suse > 0 && !ptx::mbar_wait(&s.side_empty[sb], (suse - 1) & 1, s.abort, p.err,
-                                      kErrWaitSideEmpty)) {
+      if (!load_side(p, s, t, tile, need_aux, side_tx)) {
         ok = false;
         break;
       }
-      const int64_t pos0 = static_cast<int64_t>(t) * p.tile_stride * kTileN;
-      uint8_t* slot_side = s.side + sb * kSideBytes;
-      ptx::mbar_arrive_expect_tx(&s.side_full[sb], side_tx);
-      if (need_aux) ptx::bulk_load(slot_side + kSideAuxOff, p.row_aux + pos0, 1024, &s.side_full[sb]);
-      ptx::bulk_load(slot_side + kSideIdOff, p.row_id + pos0, 1024, &s.side_full[sb]);
-      if (p.allow) ptx::bulk_load(slot_side + kSideAllowOff, p.allow + pos0 / 32, 32, &s.side_full[sb]);
       ++tile;
       // Units in MMA order: database part bp major, chunk c minor. The chunk loop is unrolled so
       // the per-chunk parameters are static-index loads, and the ring position is tracked
@@ -160,7 +169,7 @@ __device__ void run_producer(const FusedParams& p, const FusedMaps& maps, const 
       const int row = t * p.tile_stride * kTileN + static_cast<int>(rank) * kHalfN;
       for (int bp = 0; bp < p.b_parts && ok; ++bp) {
 #pragma unroll
-        for (int c = 0; c < kMaxChunks; ++c) {
+        for (int c = 0; c < kResChunks; ++c) {
           if (c >= p.nchunk) break;
           if (wrapped &&
               !ptx::mbar_wait(&s.empty[slot], phase ^ 1u, s.abort, p.err, kErrWaitSlotEmpty)) {
@@ -208,7 +217,7 @@ __device__ void run_producer(const FusedParams& p, const FusedMaps& maps, const 
 // query-lo pass (LO) and the K steps per chunk (KS: 4, 2 or 1 for chunks of 64, 32 or 16
 // columns; 0 = chunks of mixed widths, dispatched once per chunk) are template parameters, and
 // run_mma_dispatch picks the instance once per launch. Descriptors are built once per chunk and
-// kept in registers (the chunk loop is unrolled over kMaxChunks so every index is static); the
+// kept in registers (the chunk loop is unrolled over kResChunks so every index is static); the
 // ring position is tracked without division.
 constexpr uint32_t kIdesc = ptx::idesc_f16_f32(kPairQ, kTileN);
 // Descriptor address fields count 16-byte units; a K step of 16 fp16 values is 32 bytes.
@@ -284,7 +293,7 @@ __device__ void run_mma(const FusedParams& p, const Smem& s, uint32_t tmem_base)
       // lo part meets only the database hi part (bp == 0).
       for (int bp = 0; bp < p.b_parts && ok; ++bp) {
 #pragma unroll
-        for (int c = 0; c < kMaxChunks; ++c) {
+        for (int c = 0; c < kResChunks; ++c) {
           if (c >= p.nchunk) break;
           if (!ptx::mbar_wait(&s.full[slot], phase, s.abort, p.err, kErrWaitSlotFull)) {
             ok = false;
@@ -326,6 +335,127 @@ __device__ void run_mma(const FusedParams& p, const Smem& s, uint32_t tmem_base)
   }
   // Unwind: every MMA issued by this thread completes before either CTA releases TMEM or shared
   // memory (both CTAs wait for `drain`).
+  ptx::mma_commit_pair(s.drain);
+  drain_wait(s.drain, 0, p.err, s.abort);
+}
+
+// ------------------------------------------------------------------------------------------
+// Streamed query mode (large dims): every ring slot carries a database chunk together with the
+// matching chunk of this CTA's queries (hi, and lo for the database hi part when the lo pass
+// runs), so no query tile is resident. The query chunks are re-read per tile (from L2: the query
+// operand array is small next to the database), which doubles the shared-memory fill but keeps
+// any dim up to 4096 on the same kernel.
+// ------------------------------------------------------------------------------------------
+__device__ void run_producer_stream(const FusedParams& p, const FusedMaps& maps, const Smem& s,
+                                    bool lo, uint32_t rank) {
+  const bool leader = rank == 0;
+  const uint32_t full_l = ptx::peer_addr(s.full, 0);
+  uint32_t unit = 0, tile = 0;
+  uint32_t slot = 0, phase = 0;
+  bool wrapped = false;
+  const bool need_aux = p.rank_kind != kRankScaled;
+  const uint32_t side_tx = (need_aux ? 1024u : 0u) + 1024u + (p.allow ? 32u : 0u);
+  bool ok = true;
+  for (int item = first_item(); item < p.num_items && ok; item += item_step()) {
+    const Item it = item_of(p, item, rank);
+    for (int t = it.t0; t < it.t1 && ok; ++t) {
+      if (!load_side(p, s, t, tile, need_aux, side_tx)) {
+        ok = false;
+        break;
+      }
+      ++tile;
+      const int row = t * p.tile_stride * kTileN + static_cast<int>(rank) * kHalfN;
+      for (int bp = 0; bp < p.b_parts && ok; ++bp) {
+        const bool with_lo = lo && bp == 0;
+        for (int c = 0; c < p.nchunk; ++c) {
+          if (wrapped &&
+              !ptx::mbar_wait(&s.empty[slot], phase ^ 1u, s.abort, p.err, kErrWaitSlotEmpty)) {
+            ok = false;
+            break;
+          }
+          const int w = p.chunk_w[c];
+          const uint32_t a_bytes = 2u * static_cast<uint32_t>(kTileQ * w * 2);  // both CTAs
+          if (leader)
+            ptx::mbar_arrive_expect_tx(
+                &s.full[slot], static_cast<uint32_t>(kTileN * w * 2) + a_bytes * (with_lo ? 2 : 1));
+          uint8_t* sb = s.base + p.stage_off + slot * p.slot_bytes;
+          const uint32_t bar = full_l + slot * 8;
+          ptx::tma_load_2d_pair(sb, pick_map(w, &maps.b64, &maps.b32, &maps.b16),
+                                bp * p.dp + p.chunk_x[c], row, bar);
+          const CUtensorMap* am = pick_map(w, &maps.a64, &maps.a32, &maps.a16);
+          ptx::tma_load_2d_pair(sb + p.slot_a_off, am, p.chunk_x[c], it.qt * kTileQ, bar);
+          if (with_lo)
+            ptx::tma_load_2d_pair(sb + p.slot_alo_off, am, p.dp + p.chunk_x[c], it.qt * kTileQ,
+                                  bar);
+          ++unit;
+          if (++slot == static_cast<uint32_t>(p.nstages)) {
+            slot = 0;
+            phase ^= 1u;
+            wrapped = true;
+          }
+        }
+      }
+    }
+  }
+  // Unwind as run_producer: every copy landed before the CTA exits (the MMA consumed each slot's
+  // last use; side copies on this CTA's barriers).
+  const uint32_t issued = unit;
+  for (uint32_t sl = 0; sl < static_cast<uint32_t>(p.nstages) && sl < issued; ++sl) {
+    const uint32_t last = ((issued - 1 - sl) / p.nstages) * p.nstages + sl;
+    drain_wait(&s.empty[sl], (last / p.nstages) & 1, p.err, s.abort);
+  }
+  for (uint32_t sb = 0; sb < static_cast<uint32_t>(kSideBufs) && sb < tile; ++sb) {
+    const uint32_t last = ((tile - 1 - sb) / kSideBufs) * kSideBufs + sb;
+    drain_wait(&s.side_full[sb], (last / kSideBufs) & 1, p.err, s.abort);
+  }
+}
+
+template <bool LO>
+__device__ void run_mma_stream(const FusedParams& p, const Smem& s, uint32_t tmem_base) {
+  const uint32_t base_addr = ptx::smem_addr(s.base);
+  uint32_t slot = 0, phase = 0, tile = 0;
+  bool ok = true;
+  for (int item = first_item(); item < p.num_items && ok; item += item_step()) {
+    const Item it = item_of(p, item, 0);
+    for (int t = it.t0; t < it.t1 && ok; ++t) {
+      const uint32_t buf = tile & 1, use = tile >> 1;
+      if (use > 0 &&
+          !ptx::mbar_wait(&s.tempty[buf], (use - 1) & 1, s.abort, p.err, kErrWaitTmemEmpty)) {
+        ok = false;
+        break;
+      }
+      ptx::tc_fence_after();
+      const uint32_t d_tmem = tmem_base + buf * kTileN;
+      uint32_t acc = 0;
+      for (int bp = 0; bp < p.b_parts && ok; ++bp) {
+        for (int c = 0; c < p.nchunk; ++c) {
+          if (!ptx::mbar_wait(&s.full[slot], phase, s.abort, p.err, kErrWaitSlotFull)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t sb = base_addr + p.stage_off + slot * p.slot_bytes;
+          const uint32_t row_bytes = static_cast<uint32_t>(p.chunk_w[c] * 2);
+          const uint64_t ah = ptx::smem_desc(sb + p.slot_a_off, row_bytes);
+          const uint64_t al = ptx::smem_desc(sb + p.slot_alo_off, row_bytes);
+          const uint64_t bd = ptx::smem_desc(sb, row_bytes);
+          if (LO && bp == 0)
+            issue_chunk<true, 0>(d_tmem, ah, al, bd, acc, p.chunk_w[c] / 16);
+          else
+            issue_chunk<false, 0>(d_tmem, ah, al, bd, acc, p.chunk_w[c] / 16);
+          acc = 1;
+          ptx::mma_commit_pair(&s.empty[slot]);
+          if (++slot == static_cast<uint32_t>(p.nstages)) {
+            slot = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) break;
+      ptx::mma_commit_pair(&s.tfull[buf]);
+      ++tile;
+    }
+  }
   ptx::mma_commit_pair(s.drain);
   drain_wait(s.drain, 0, p.err, s.abort);
 }
@@ -761,9 +891,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFusedThreads, 1)
   const bool lo = p.query_split != 0 && *p.q_lo_flag != 0;
 
   if (warp == kEpiWarps) {
-    if (lane == 0) run_producer(p, maps, s, lo, rank);
+    if (lane == 0) {
+      if (p.a_stream)
+        run_producer_stream(p, maps, s, lo, rank);
+      else
+        run_producer(p, maps, s, lo, rank);
+    }
   } else if (warp == kEpiWarps + 1) {
-    if (lane == 0 && rank == 0) run_mma_dispatch(p, s, tmem_base, lo);
+    if (lane == 0 && rank == 0) {
+      if (!p.a_stream)
+        run_mma_dispatch(p, s, tmem_base, lo);
+      else if (lo)
+        run_mma_stream<true>(p, s, tmem_base);
+      else
+        run_mma_stream<false>(p, s, tmem_base);
+    }
     __syncwarp();
   } else {
     run_epilogue<KL>(p, s, tmem_base, rank);
@@ -822,31 +964,59 @@ int fused_max_pairs(int smem_bytes) {
 }
 
 bool plan_fused_smem(FusedParams& p, int max_smem_optin) {
-  int off = 0;
-  for (int part = 0; part < 2; ++part) {
-    p.a_tx_bytes[part] = 0;
-    for (int c = 0; c < p.nchunk; ++c) {
-      const int bytes = kTileQ * p.chunk_w[c] * 2;
-      p.a_off[part][c] = off;
-      off += (bytes + 1023) & ~1023;
-      p.a_tx_bytes[part] += bytes;
-    }
-  }
-  p.side_off = off;
-  off += kSideBufs * kSideBytes;
-  p.defer_off = off;
-  off += kEpiWarps * 32 * kDeferStride * 4;
-  off = (off + 1023) & ~1023;  // stages stay 1024-aligned (128-byte swizzle)
-  p.stage_off = off;
   const int budget = max_smem_optin - 1024;  // alignment slack
   auto bar_bytes = [](int stages) { return (2 * stages + 7 + 2 * kSideBufs) * 8 + 16; };
-  int stages = kMaxStages;
-  for (; stages >= 2; --stages) {
-    if (off + stages * kUnitBytes + bar_bytes(stages) <= budget) break;
+  // Side ring + deferred rows, then the ring (1024-aligned for the 128-byte swizzle).
+  auto tail_from = [&](int off) {
+    p.side_off = off;
+    off += kSideBufs * kSideBytes;
+    p.defer_off = off;
+    off += kEpiWarps * 32 * kDeferStride * 4;
+    return (off + 1023) & ~1023;
+  };
+  auto ring = [&](int off, int slot_bytes) {
+    int stages = kMaxStages;
+    while (stages >= 2 && off + stages * slot_bytes + bar_bytes(stages) > budget) --stages;
+    return stages;
+  };
+  // Resident query tile (both parts) when it fits with at least two ring slots.
+  if (p.nchunk <= kResChunks) {
+    int off = 0;
+    for (int part = 0; part < 2; ++part) {
+      p.a_tx_bytes[part] = 0;
+      for (int c = 0; c < p.nchunk; ++c) {
+        const int bytes = kTileQ * p.chunk_w[c] * 2;
+        p.a_off[part][c] = off;
+        off += (bytes + 1023) & ~1023;
+        p.a_tx_bytes[part] += bytes;
+      }
+    }
+    off = tail_from(off);
+    const int stages = ring(off, kUnitBytes);
+    if (stages >= 2) {
+      p.a_stream = 0;
+      p.slot_bytes = kUnitBytes;
+      p.slot_a_off = p.slot_alo_off = 0;
+      p.stage_off = off;
+      p.nstages = stages;
+      p.bar_off = off + stages * kUnitBytes;
+      p.smem_bytes = p.bar_off + bar_bytes(stages) + 1024;
+      return true;
+    }
   }
+  // Streamed: each slot = database chunk + query hi chunk + query lo chunk (16 KB each).
+  const int off = tail_from(0);
+  const int slot_bytes = kUnitBytes + 2 * (kTileQ * 64 * 2);
+  const int stages = ring(off, slot_bytes);
   if (stages < 2) return false;
+  p.a_stream = 1;
+  p.slot_bytes = slot_bytes;
+  p.slot_a_off = kUnitBytes;
+  p.slot_alo_off = kUnitBytes + kTileQ * 64 * 2;
+  p.a_tx_bytes[0] = p.a_tx_bytes[1] = 0;
+  p.stage_off = off;
   p.nstages = stages;
-  p.bar_off = off + stages * kUnitBytes;
+  p.bar_off = off + stages * slot_bytes;
   p.smem_bytes = p.bar_off + bar_bytes(stages) + 1024;
   return true;
 }

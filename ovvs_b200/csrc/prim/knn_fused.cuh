@@ -57,7 +57,8 @@ constexpr int kPartCols = 128;             // columns per epilogue warp (a part 
 constexpr int kListsPerItem = kEpiWarps / 4;  // list-mode output: one sorted list per column part
 constexpr int kFusedThreads = 32 * (kEpiWarps + 2);  // epilogue warps, then TMA, then MMA
 constexpr int kMaxStages = 16;             // smem ring slots at most
-constexpr int kMaxChunks = 8;              // padded dim <= 512 per part
+constexpr int kMaxChunks = 66;             // padded dim <= 4096 per part (64 + 32/16 tails)
+constexpr int kResChunks = 8;              // resident query tile: at most 8 chunks per part
 constexpr int kTmemCols = 512;             // two 256-column fp32 accumulators
 constexpr int kSideBufs = 4;               // side ring depth (tiles)
 constexpr int kSideAuxOff = 0;             // side slot: aux[256] fp32
@@ -88,7 +89,14 @@ struct FusedParams {
   int nchunk;                      // K chunks per part
   int chunk_x[kMaxChunks];         // first column of each chunk within a part
   int chunk_w[kMaxChunks];         // chunk width in fp16 elements: 64, 32 or 16
-  int a_off[2][kMaxChunks];        // smem byte offset of query chunk (part, chunk)
+  int a_off[2][kResChunks];        // resident mode: smem byte offset of query chunk (part, chunk)
+  // Streamed mode (a_stream = 1, when the resident query tile does not fit shared memory, i.e.
+  // large dims): each ring slot holds a database chunk at +0, the matching query hi chunk at
+  // slot_a_off and lo chunk at slot_alo_off, slots slot_bytes apart; no resident query tile.
+  int a_stream;
+  int slot_bytes;
+  int slot_a_off;
+  int slot_alo_off;
   int a_tx_bytes[2];               // bytes of one query part (all chunks)
   int b_parts;                     // 1: rows fp16-exact; 2: rows split hi + lo
   int nunits;                      // smem units per database tile = b_parts * nchunk

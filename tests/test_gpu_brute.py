@@ -112,6 +112,20 @@ def test_dims_and_chunking(dim, ovvs, gpu, oracle):
     _run_parity(ovvs, gpu, oracle, "l2", "f32", n=1700, dim=dim, nq=130, k=7, seed=dim)
 
 
+@pytest.mark.parametrize("metric,dtype,dim", [
+    ("l2", "f32", 320), ("l2", "f16", 384), ("inner_product", "f32", 512),
+    ("cosine", "f32", 768), ("l2", "f32", 1000), ("inner_product", "f16", 1536),
+    ("l2", "f16", 2048)])
+def test_large_dims_streamed_queries(metric, dtype, dim, ovvs, gpu, oracle):
+    """Dims whose 128-query tile does not fit shared memory with the ring run the fused kernel's
+    streamed-query mode (query chunks travel with each database chunk)."""
+    _run_parity(ovvs, gpu, oracle, metric, dtype, n=2500, dim=dim, nq=150, k=9, seed=dim)
+
+
+def test_max_dim_4096(ovvs, gpu, oracle):
+    _run_parity(ovvs, gpu, oracle, "l2", "f32", n=600, dim=4096, nq=40, k=5, seed=4096)
+
+
 @pytest.mark.parametrize("n,nq,k", [(1, 1, 1), (3, 2, 5), (255, 129, 16), (256, 128, 28),
                                     (257, 127, 3), (513, 1, 1), (1000, 300, 20)])
 def test_ragged_sizes(n, nq, k, ovvs, gpu, oracle):
