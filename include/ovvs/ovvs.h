@@ -257,26 +257,46 @@ OVVS_API ovvsStatus ovvsPqAdcBatch(ovvsResources_t res, const float* tables, int
 OVVS_API ovvsStatus ovvsProbeJson(char* buf, int32_t len);
 
 /* ------------------------------------------------------------------------------------------ */
-/* Primitives (reference src/rt/resources.cpp:178-216). Exported; UNSUPPORTED in this build:   */
-/* their device versions are the next scope after the brute-force path.                         */
+/* Primitives (reference src/rt/resources.cpp:178-216) on the device. Host buffers in and out.  */
+/* Results equal the reference's CPU path bit for bit: every output element sums its products  */
+/* in k order with separately rounded multiply and add (Lp distances use the device powf and    */
+/* may differ by an ulp). Null pointers or non-positive sizes: OVVS_STATUS_INVALID_ARGUMENT.    */
 /* ------------------------------------------------------------------------------------------ */
 
+/* C[m x n] = A[m x k] * (trans_b ? B[n x k]^T : B[k x n]), row-major, fp32. */
 OVVS_API ovvsStatus ovvsGemm(ovvsResources_t res, const float* a, const float* b, float* c,
                              int64_t m, int64_t n, int64_t k, int32_t trans_b);
+/* compute F16 rounds A and B to half before the products (the products are exact in fp32);
+   any other type computes in F32. ovvsResourcesLastComputeDtype reports which ran. */
 OVVS_API ovvsStatus ovvsGemmEx(ovvsResources_t res, const float* a, const float* b, float* c,
                                int64_t m, int64_t n, int64_t k, int32_t trans_b,
                                ovvsDType compute);
+/* Per row the min(k, cols) smallest (largest != 0: largest) scores, ascending (descending),
+   ties by lower column, NaN after every number; indices / values are [rows][min(k, cols)]. */
 OVVS_API ovvsStatus ovvsTopk(ovvsResources_t res, const float* scores, int64_t rows,
                              int64_t cols, int64_t k, int64_t* indices, float* values,
                              int32_t largest);
+/* out[i] = src[idx[i]]; an idx outside [0, src_rows) gives a row of zeros. */
 OVVS_API ovvsStatus ovvsGatherRows(ovvsResources_t res, const float* src, int64_t src_rows,
                                    int64_t dim, const int64_t* idx, int64_t nidx, float* out);
+/* out[nx][ny]: L2_EXPANDED (squared), INNER_PRODUCT (negated dot), COSINE_EXPANDED through
+   norms and the GEMM; L2_SQRT, HAMMING (sign-bit mismatches), LP (p = metric_arg > 0 ?
+   metric_arg : 2) per pair. */
 OVVS_API ovvsStatus ovvsPairwiseDistance(ovvsResources_t res, ovvsMetric metric, const float* x,
                                          int64_t nx, const float* y, int64_t ny, int64_t dim,
                                          float* out, float metric_arg);
+/* Same as ovvsTopk. */
 OVVS_API ovvsStatus ovvsKSelection(ovvsResources_t res, const float* scores, int64_t rows,
                                    int64_t cols, int64_t k, int64_t* indices, float* values,
                                    int32_t largest);
+
+/* Exact all-pairs kNN graph on the device (reference src/neighbors/graphs.cpp:3384-3396): per
+   row the min(k, n - 1) nearest other rows under ovvsPairwiseDistance's scores (LP with p = 2),
+   ascending, ties by lower row; INNER_PRODUCT distances are the dot products. n <= 1 or k <= 0:
+   OVVS_STATUS_INVALID_ARGUMENT. */
+OVVS_API ovvsStatus ovvsAllNeighbors(ovvsResources_t res, const float* dataset, int64_t n,
+                                     int64_t dim, ovvsMetric metric, int32_t k,
+                                     int64_t* neighbors, float* distances);
 
 /* ------------------------------------------------------------------------------------------ */
 /* Exact brute-force kNN  (reference src/neighbors/indexes.cpp:236-268)                         */
@@ -426,10 +446,6 @@ OVVS_API ovvsStatus ovvsScannSearch(ovvsResources_t res, ovvsScannIndex_t index,
                                     const float* queries, int64_t nq, int64_t k, int32_t nprobe,
                                     int32_t krefine, int64_t* neighbors, float* distances);
 OVVS_API ovvsStatus ovvsScannDestroy(ovvsScannIndex_t index);
-
-OVVS_API ovvsStatus ovvsAllNeighbors(ovvsResources_t res, const float* dataset, int64_t n,
-                                     int64_t dim, ovvsMetric metric, int32_t k,
-                                     int64_t* neighbors, float* distances);
 
 /* ------------------------------------------------------------------------------------------ */
 /* Allow-list bitset  (reference src/rt/resources.cpp:218-229)                                 */

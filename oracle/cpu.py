@@ -71,6 +71,12 @@ class Oracle:
                                       c_int64, POINTER(c_float), c_float]
         L.oracle_topk.argtypes = [POINTER(c_float), c_int64, c_int64, c_int64, POINTER(c_int64),
                                   POINTER(c_float), c_int32]
+        L.oracle_gemm.argtypes = [POINTER(c_float), POINTER(c_float), POINTER(c_float), c_int64,
+                                  c_int64, c_int64, c_int32, c_int32]
+        L.oracle_gather_rows.argtypes = [POINTER(c_float), c_int64, c_int64, POINTER(c_int64),
+                                         c_int64, POINTER(c_float)]
+        L.oracle_all_neighbors.argtypes = [POINTER(c_float), c_int64, c_int64, c_int32, c_int32,
+                                           POINTER(c_int64), POINTER(c_float), c_int32]
         L.oracle_brute_search.argtypes = [POINTER(c_float), c_int64, c_int64, c_int32,
                                           POINTER(c_float), c_int64, c_int64, POINTER(c_uint8),
                                           POINTER(c_int64), POINTER(c_float), c_int32]
@@ -122,6 +128,31 @@ class Oracle:
         self.lib.oracle_topk(_ptr(scores, c_float), rows, cols, k, _ptr(idx, c_int64),
                              _ptr(val, c_float), int(largest))
         return idx, val
+
+    def gemm(self, a, b, m, n, k, trans_b=True, round_f16=False):
+        a, b = _f32(a).reshape(-1), _f32(b).reshape(-1)
+        c = np.empty((m, n), np.float32)
+        self.lib.oracle_gemm(_ptr(a, c_float), _ptr(b, c_float), _ptr(c, c_float), m, n, k,
+                             int(bool(trans_b)), int(bool(round_f16)))
+        return c
+
+    def gather_rows(self, src, indices):
+        src = _f32(src)
+        ix = np.ascontiguousarray(indices, np.int64)
+        out = np.empty((ix.size, src.shape[1]), np.float32)
+        self.lib.oracle_gather_rows(_ptr(src, c_float), src.shape[0], src.shape[1],
+                                    _ptr(ix, c_int64), ix.size, _ptr(out, c_float))
+        return out
+
+    def all_neighbors(self, data, k, metric="l2"):
+        data = _f32(data)
+        n, dim = data.shape
+        ke = min(k, n - 1)
+        nb = np.empty((n, ke), np.int64)
+        ds = np.empty((n, ke), np.float32)
+        self.lib.oracle_all_neighbors(_ptr(data, c_float), n, dim, METRICS.get(metric, metric), k,
+                                      _ptr(nb, c_int64), _ptr(ds, c_float), self.nthreads)
+        return nb, ds
 
     def brute_search(self, data, queries, k, metric="l2", bitset=None, out_fill=None,
                      nthreads=None):
@@ -213,6 +244,15 @@ class Reference:
         L.ovvsBitsetFromAllowList.argtypes = [c_int64, POINTER(c_int64), c_int64, POINTER(c_uint8)]
         L.ovvsTopk.argtypes = [c_void_p, POINTER(c_float), c_int64, c_int64, c_int64,
                                POINTER(c_int64), POINTER(c_float), c_int32]
+        L.ovvsGemm.argtypes = [c_void_p, POINTER(c_float), POINTER(c_float), POINTER(c_float),
+                               c_int64, c_int64, c_int64, c_int32]
+        L.ovvsGatherRows.argtypes = [c_void_p, POINTER(c_float), c_int64, c_int64,
+                                     POINTER(c_int64), c_int64, POINTER(c_float)]
+        L.ovvsPairwiseDistance.argtypes = [c_void_p, c_int32, POINTER(c_float), c_int64,
+                                           POINTER(c_float), c_int64, c_int64, POINTER(c_float),
+                                           c_float]
+        L.ovvsAllNeighbors.argtypes = [c_void_p, POINTER(c_float), c_int64, c_int64, c_int32,
+                                       c_int32, POINTER(c_int64), POINTER(c_float)]
 
     def resources(self):
         r = c_void_p()
@@ -290,6 +330,49 @@ class Reference:
                                  _ptr(val, c_float), int(largest)) == 0
         self.lib.ovvsResourcesDestroy(res)
         return idx, val
+
+
+    def gemm(self, a, b, m, n, k, trans_b=True):
+        a, b = _f32(a).reshape(-1), _f32(b).reshape(-1)
+        c = np.empty((m, n), np.float32)
+        res = self.resources()
+        assert self.lib.ovvsGemm(res, _ptr(a, c_float), _ptr(b, c_float), _ptr(c, c_float), m, n,
+                                 k, int(bool(trans_b))) == 0
+        self.lib.ovvsResourcesDestroy(res)
+        return c
+
+    def gather_rows(self, src, indices):
+        src = _f32(src)
+        ix = np.ascontiguousarray(indices, np.int64)
+        out = np.empty((ix.size, src.shape[1]), np.float32)
+        res = self.resources()
+        assert self.lib.ovvsGatherRows(res, _ptr(src, c_float), src.shape[0], src.shape[1],
+                                       _ptr(ix, c_int64), ix.size, _ptr(out, c_float)) == 0
+        self.lib.ovvsResourcesDestroy(res)
+        return out
+
+    def pairwise(self, metric, x, y, metric_arg=2.0):
+        x, y = _f32(x), _f32(y)
+        out = np.empty((x.shape[0], y.shape[0]), np.float32)
+        res = self.resources()
+        assert self.lib.ovvsPairwiseDistance(res, METRICS.get(metric, metric), _ptr(x, c_float),
+                                             x.shape[0], _ptr(y, c_float), y.shape[0], x.shape[1],
+                                             _ptr(out, c_float), metric_arg) == 0
+        self.lib.ovvsResourcesDestroy(res)
+        return out
+
+    def all_neighbors(self, data, k, metric="l2"):
+        data = _f32(data)
+        n, dim = data.shape
+        ke = min(k, n - 1)
+        nb = np.empty((n, ke), np.int64)
+        ds = np.empty((n, ke), np.float32)
+        res = self.resources()
+        assert self.lib.ovvsAllNeighbors(res, _ptr(data, c_float), n, dim,
+                                         METRICS.get(metric, metric), k, _ptr(nb, c_int64),
+                                         _ptr(ds, c_float)) == 0
+        self.lib.ovvsResourcesDestroy(res)
+        return nb, ds
 
 
 def make_data(n: int, dim: int, seed: int) -> np.ndarray:

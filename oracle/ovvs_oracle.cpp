@@ -277,6 +277,51 @@ void oracle_brute_search(const float* data, int64_t n, int64_t dim, int32_t metr
     for (int64_t i = 0; i < nq * k; ++i) distances[i] = -distances[i];
 }
 
+void oracle_gemm(const float* a, const float* b, float* c, int64_t m, int64_t n, int64_t k,
+                 int32_t trans_b, int32_t round_f16) {
+  /* cpu_prims.cpp:48-58 naive loop; round_f16 rounds each operand to half (RNE) first. */
+  auto op = [round_f16](float v) {
+    return round_f16 ? oracle_f16_to_f32(oracle_f32_to_f16_rne(v)) : v;
+  };
+  for (int64_t i = 0; i < m; ++i) {
+    for (int64_t j = 0; j < n; ++j) {
+      float s = 0.f;
+      for (int64_t t = 0; t < k; ++t)
+        s += op(a[i * k + t]) * op(trans_b ? b[j * k + t] : b[t * n + j]);
+      c[i * n + j] = s;
+    }
+  }
+}
+
+void oracle_gather_rows(const float* src, int64_t src_rows, int64_t dim, const int64_t* idx,
+                        int64_t nidx, float* out) {
+  /* cpu_prims.cpp:108-118 */
+  for (int64_t i = 0; i < nidx; ++i) {
+    const int64_t r = idx[i];
+    for (int64_t d = 0; d < dim; ++d)
+      out[i * dim + d] = (r >= 0 && r < src_rows) ? src[r * dim + d] : 0.f;
+  }
+}
+
+void oracle_all_neighbors(const float* data, int64_t n, int64_t dim, int32_t metric, int32_t k,
+                          int64_t* neighbors, float* distances, int32_t nthreads) {
+  /* graphs.cpp:3384-3396: pairwise (metric_arg 2), diagonal +inf, k = min(k, n - 1) smallest. */
+  std::vector<float> ynorm(static_cast<size_t>(n));
+  for (int64_t j = 0; j < n; ++j) ynorm[static_cast<size_t>(j)] = nrm2sq_seq(data + j * dim, dim);
+  const int64_t ke = std::min<int64_t>(k, n - 1);
+  const float inf = std::numeric_limits<float>::infinity();
+  parallel_for(n, nthreads, [&](int64_t q0, int64_t q1) {
+    std::vector<float> scores(static_cast<size_t>(n));
+    for (int64_t i = q0; i < q1; ++i) {
+      pairwise_block(metric, data + i * dim, 1, data, n, dim, ynorm.data(), scores.data(), 2.f);
+      scores[static_cast<size_t>(i)] = inf;
+      topk_rows(scores.data(), 1, n, ke, neighbors + i * ke, distances + i * ke, false);
+    }
+  });
+  if (metric == kIP)
+    for (int64_t i = 0; i < n * ke; ++i) distances[i] = -distances[i];
+}
+
 int32_t oracle_kmeans_init_rows(int64_t n, int32_t k, int64_t* rows) {
   /* mixer.cpp:879-890: std::mt19937(42), uniform_int_distribution<int64_t>(0, n-1), up to 8
      redraws when the row was already used. */

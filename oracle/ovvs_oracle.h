@@ -34,6 +34,19 @@ void oracle_pairwise(int32_t metric, const float* x, int64_t nx, const float* y,
 void oracle_topk(const float* scores, int64_t rows, int64_t cols, int64_t k, int64_t* indices,
                  float* values, int32_t largest);
 
+/* cpu_prims.cpp:48-58 cpu_gemm (the naive loop: sequential fp32, separate multiply and add).
+   round_f16: operands rounded to half first (the F16 compute type of ovvsGemmEx). */
+void oracle_gemm(const float* a, const float* b, float* c, int64_t m, int64_t n, int64_t k,
+                 int32_t trans_b, int32_t round_f16);
+
+/* cpu_prims.cpp:108-118 cpu_gather_rows (out-of-range index -> zero row). */
+void oracle_gather_rows(const float* src, int64_t src_rows, int64_t dim, const int64_t* idx,
+                        int64_t nidx, float* out);
+
+/* graphs.cpp:3384-3396 ovvsAllNeighbors; outputs [n x min(k, n - 1)]. */
+void oracle_all_neighbors(const float* data, int64_t n, int64_t dim, int32_t metric, int32_t k,
+                          int64_t* neighbors, float* distances, int32_t nthreads);
+
 /* mixer.cpp:843-864 brute_search_impl (blocked over queries; same per-element arithmetic).
    nthreads > 1 splits queries across threads (results identical). */
 void oracle_brute_search(const float* data, int64_t n, int64_t dim, int32_t metric,

@@ -80,6 +80,20 @@ def _bind(lib):
                               c_int32),
         "ovvsBatcherLastBatchSize": ([c_void_p, P(c_int32)], c_int32),
         "ovvsBatcherDestroy": ([c_void_p], c_int32),
+        "ovvsGemm": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                      c_int32], c_int32),
+        "ovvsGemmEx": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                        c_int32, c_int32], c_int32),
+        "ovvsTopk": ([c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p,
+                      c_int32], c_int32),
+        "ovvsKSelection": ([c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p,
+                            c_int32], c_int32),
+        "ovvsGatherRows": ([c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_void_p],
+                           c_int32),
+        "ovvsPairwiseDistance": ([c_void_p, c_int32, c_void_p, c_int64, c_void_p, c_int64,
+                                  c_int64, c_void_p, c_float], c_int32),
+        "ovvsAllNeighbors": ([c_void_p, c_void_p, c_int64, c_int64, c_int32, c_int32, c_void_p,
+                              c_void_p], c_int32),
         # extensions (include/ovvs/ovvs_cuda.h)
         "ovvsResourcesStream": ([c_void_p, P(c_void_p)], c_int32),
         "ovvsResourcesSynchronize": ([c_void_p], c_int32),
@@ -225,6 +239,75 @@ class Resources:
         ms = (c_float * 4)()
         _check(lib().ovvsResourcesLastPhaseMs(self._h, ms, 4), "phase times")
         return list(ms)
+
+    # Primitives (reference python/ovvs/__init__.py Resources.gemm / topk / gather_rows, which
+    # return flat lists; these return numpy arrays of the same values, shaped [rows, cols]).
+    def gemm(self, a, b, m, n, k, trans_b=1, compute_dtype=0) -> np.ndarray:
+        """C[m, n] = A[m, k] @ (B[n, k].T if trans_b else B[k, n]) (ovvsGemm / ovvsGemmEx)."""
+        a = np.ascontiguousarray(a, np.float32).reshape(-1)
+        b = np.ascontiguousarray(b, np.float32).reshape(-1)
+        if a.size < m * k or b.size < k * n:
+            raise ValueError("gemm operands are smaller than m*k / k*n")
+        c = np.empty((m, n), np.float32)
+        if compute_dtype:
+            st = lib().ovvsGemmEx(self._h, _ptr(a), _ptr(b), _ptr(c), m, n, k, int(trans_b),
+                                  int(compute_dtype))
+        else:
+            st = lib().ovvsGemm(self._h, _ptr(a), _ptr(b), _ptr(c), m, n, k, int(trans_b))
+        _check(st, "gemm")
+        return c
+
+    def topk(self, scores, rows, cols, k, largest=0):
+        """(indices [rows, min(k, cols)], values) of each row's k smallest (largest) scores."""
+        s = np.ascontiguousarray(scores, np.float32).reshape(-1)
+        if s.size < rows * cols:
+            raise ValueError("scores is smaller than rows*cols")
+        ke = min(k, cols)
+        idx = np.empty((rows, ke), np.int64)
+        val = np.empty((rows, ke), np.float32)
+        _check(lib().ovvsTopk(self._h, _ptr(s), rows, cols, k, _ptr(idx), _ptr(val),
+                              int(largest)), "topk")
+        return idx, val
+
+    def k_selection(self, scores, rows, cols, k, largest=0):
+        return self.topk(scores, rows, cols, k, largest)
+
+    def gather_rows(self, src, src_rows, dim, indices) -> np.ndarray:
+        """out[i] = src[indices[i]] (zeros for an index outside [0, src_rows))."""
+        s = np.ascontiguousarray(src, np.float32).reshape(-1)
+        if s.size < src_rows * dim:
+            raise ValueError("src is smaller than src_rows*dim")
+        ix = np.ascontiguousarray(indices, np.int64).reshape(-1)
+        out = np.empty((ix.size, dim), np.float32)
+        _check(lib().ovvsGatherRows(self._h, _ptr(s), src_rows, dim, _ptr(ix), ix.size,
+                                    _ptr(out)), "gather rows")
+        return out
+
+    def pairwise_distance(self, x, y, metric="l2", metric_arg=2.0) -> np.ndarray:
+        """[nx, ny] scores of ovvsPairwiseDistance."""
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.ascontiguousarray(y, np.float32)
+        if x.ndim != 2 or y.ndim != 2 or x.shape[1] != y.shape[1]:
+            raise ValueError("x and y must be 2-D with the same dim")
+        m = METRIC[metric] if isinstance(metric, str) else int(metric)
+        out = np.empty((x.shape[0], y.shape[0]), np.float32)
+        _check(lib().ovvsPairwiseDistance(self._h, m, _ptr(x), x.shape[0], _ptr(y), y.shape[0],
+                                          x.shape[1], _ptr(out), float(metric_arg)),
+               "pairwise distance")
+        return out
+
+    def all_neighbors(self, dataset, k, metric="l2"):
+        """Exact kNN graph (ovvsAllNeighbors): (neighbors, distances), [n, min(k, n - 1)]."""
+        a = np.ascontiguousarray(dataset, np.float32)
+        if a.ndim != 2:
+            raise ValueError("dataset must be 2-D [n, dim]")
+        m = METRIC[metric] if isinstance(metric, str) else int(metric)
+        ke = max(0, min(int(k), a.shape[0] - 1))
+        nb = np.empty((a.shape[0], ke), np.int64)
+        ds = np.empty((a.shape[0], ke), np.float32)
+        _check(lib().ovvsAllNeighbors(self._h, _ptr(a), a.shape[0], a.shape[1], m, int(k),
+                                      _ptr(nb), _ptr(ds)), "all neighbors")
+        return nb, ds
 
     def last_kernel_error(self) -> int:
         """Watchdog code seen by the last synchronising call that failed (0 if none); clears it."""

@@ -1,40 +1,10 @@
 // Entry points of the ovvs ABI outside this library's scope (IVF, graph indexes, quantizers,
-// PCA, SLINK/spectral, the non-kNN primitives). They exist so that binaries and bindings built
+// PCA, SLINK/spectral). They exist so that binaries and bindings built
 // against the reference ABI still link and load; each returns OVVS_STATUS_UNSUPPORTED (Destroy
 // functions accept any handle, as none can have been created, and return OVVS_STATUS_SUCCESS).
 #include "ovvs/ovvs.h"
 
 extern "C" {
-
-ovvsStatus ovvsGemm(ovvsResources_t res, const float* a, const float* b, float* c, int64_t m, int64_t n, int64_t k, int32_t trans_b) {
-  (void)res; (void)a; (void)b; (void)c; (void)m; (void)n; (void)k; (void)trans_b;
-  return OVVS_STATUS_UNSUPPORTED;
-}
-
-ovvsStatus ovvsGemmEx(ovvsResources_t res, const float* a, const float* b, float* c, int64_t m, int64_t n, int64_t k, int32_t trans_b, ovvsDType compute) {
-  (void)res; (void)a; (void)b; (void)c; (void)m; (void)n; (void)k; (void)trans_b; (void)compute;
-  return OVVS_STATUS_UNSUPPORTED;
-}
-
-ovvsStatus ovvsTopk(ovvsResources_t res, const float* scores, int64_t rows, int64_t cols, int64_t k, int64_t* indices, float* values, int32_t largest) {
-  (void)res; (void)scores; (void)rows; (void)cols; (void)k; (void)indices; (void)values; (void)largest;
-  return OVVS_STATUS_UNSUPPORTED;
-}
-
-ovvsStatus ovvsGatherRows(ovvsResources_t res, const float* src, int64_t src_rows, int64_t dim, const int64_t* idx, int64_t nidx, float* out) {
-  (void)res; (void)src; (void)src_rows; (void)dim; (void)idx; (void)nidx; (void)out;
-  return OVVS_STATUS_UNSUPPORTED;
-}
-
-ovvsStatus ovvsPairwiseDistance(ovvsResources_t res, ovvsMetric metric, const float* x, int64_t nx, const float* y, int64_t ny, int64_t dim, float* out, float metric_arg) {
-  (void)res; (void)metric; (void)x; (void)nx; (void)y; (void)ny; (void)dim; (void)out; (void)metric_arg;
-  return OVVS_STATUS_UNSUPPORTED;
-}
-
-ovvsStatus ovvsKSelection(ovvsResources_t res, const float* scores, int64_t rows, int64_t cols, int64_t k, int64_t* indices, float* values, int32_t largest) {
-  (void)res; (void)scores; (void)rows; (void)cols; (void)k; (void)indices; (void)values; (void)largest;
-  return OVVS_STATUS_UNSUPPORTED;
-}
 
 ovvsStatus ovvsIvfFlatBuild(ovvsResources_t res, const float* dataset, int64_t n, int64_t dim, ovvsMetric metric, int32_t nlist, ovvsIvfFlatIndex_t* index) {
   (void)res; (void)dataset; (void)n; (void)dim; (void)metric; (void)nlist; (void)index;
@@ -304,11 +274,6 @@ ovvsStatus ovvsScannSearch(ovvsResources_t res, ovvsScannIndex_t index, const fl
 ovvsStatus ovvsScannDestroy(ovvsScannIndex_t index) {
   (void)index;
   return OVVS_STATUS_SUCCESS;
-}
-
-ovvsStatus ovvsAllNeighbors(ovvsResources_t res, const float* dataset, int64_t n, int64_t dim, ovvsMetric metric, int32_t k, int64_t* neighbors, float* distances) {
-  (void)res; (void)dataset; (void)n; (void)dim; (void)metric; (void)k; (void)neighbors; (void)distances;
-  return OVVS_STATUS_UNSUPPORTED;
 }
 
 ovvsStatus ovvsSlinkFit(ovvsResources_t res, const float* dataset, int64_t n, int64_t dim, int32_t nclusters, int32_t knn, ovvsSlinkModel_t* model) {

@@ -68,3 +68,8 @@ def gpu(ovvs):
     assert res.gpu_available(), "GPU tests need an sm_100 device (B200)"
     yield res
     res.close()
+
+
+@pytest.fixture(scope="session")
+def golden_prims():
+    return _load_npz_cases("prims.npz")

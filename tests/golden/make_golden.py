@@ -131,6 +131,76 @@ def kmeans_cases(rng):
     return cases
 
 
+def prims_cases(rng):
+    """Inputs of the primitive entry points (resources.cpp:178-216) and ovvsAllNeighbors
+    (graphs.cpp:3384-3396): odd shapes, the top-k edge values, out-of-range gather indices,
+    every metric (and an unknown one), duplicate rows."""
+    gemm = [
+        ("gemm_small_nt", rng.standard_normal((5, 3)), rng.standard_normal((3, 7)), 0),
+        ("gemm_small_t", rng.standard_normal((5, 3)), rng.standard_normal((7, 3)), 1),
+        ("gemm_odd_t", make_data(33, 129, 11), make_data(65, 129, 12), 1),
+        ("gemm_odd_nt", make_data(31, 70, 13), make_data(70, 17, 14), 0),
+        ("gemm_k1", rng.standard_normal((4, 1)), rng.standard_normal((1, 6)), 0),
+        ("gemm_cancel", np.array([[1e8, 1.0, -1e8]]), np.array([[1.0, 1.0, 1.0], [1.0, 0.5, 1.0]]), 1),
+    ]
+    edge = np.array([[np.nan, 0.0, -0.0, np.inf, -np.inf, 1.0, 1.0, np.nan],
+                     [2.0, -1.0, 2.0, -1.0, np.nan, 0.0, -0.0, 3.0]], np.float32)
+    ties = rng.integers(-5, 5, (50, 300)).astype(np.float32)
+    topk = [("topk_edge_small", edge, 8, 0), ("topk_edge_large", edge, 8, 1),
+            ("topk_k_gt_cols", edge, 10, 0), ("topk_ties_small", ties, 17, 0),
+            ("topk_ties_large", ties, 17, 1), ("topk_k1", rng.standard_normal((7, 1000)), 1, 1)]
+    gather = [("gather_mixed", rng.standard_normal((10, 5)), np.array([3, -1, 9, 10, 0, 3, 9]))]
+    x = make_data(13, 19, 21)
+    y = make_data(29, 19, 22)
+    signs = rng.choice(np.array([-1.0, -0.0, 0.0, 1.0], np.float32), (29, 19))
+    pairwise = [(f"pw_{m}", x, y, m, 2.0) for m in ("l2", "l2_sqrt", "inner_product", "cosine",
+                                                   "hamming", "lp", "unknown7")]
+    pairwise += [("pw_lp3", x, y, "lp", 3.0), ("pw_lp0", x, y, "lp", 0.0),
+                 ("pw_lp1", x, y, "lp", 1.0), ("pw_hamming_zeros", signs[:11], signs, "hamming", 2.0),
+                 ("pw_cos_zero_row", np.vstack([x[:3], np.zeros((1, 19))]), y, "cosine", 2.0)]
+    base = make_data(200, 16, 31)
+    dup = np.repeat(make_data(40, 8, 32), 3, axis=0)
+    allnb = [(f"an_{m}", base, m, 7) for m in ("l2", "l2_sqrt", "inner_product", "cosine",
+                                              "hamming", "lp")]
+    allnb += [("an_dup_l2", dup, "l2", 5), ("an_dup_ip", dup, "inner_product", 4),
+              ("an_k_gt_n", make_data(2, 4, 33), "l2", 3),
+              ("an_ip_full", make_data(9, 4, 34), "inner_product", 8)]
+    return gemm, topk, gather, pairwise, allnb
+
+
+def write_prims(ref, rng):
+    gemm, topk, gather, pairwise, allnb = prims_cases(rng)
+    out = {}
+    for name, a, b, tb in gemm:
+        a = np.ascontiguousarray(a, np.float32)
+        b = np.ascontiguousarray(b, np.float32)
+        m, k = a.shape
+        n = b.shape[0] if tb else b.shape[1]
+        out[name + "__a"], out[name + "__b"], out[name + "__trans_b"] = a, b, np.array(tb)
+        out[name + "__c"] = ref.gemm(a, b, m, n, k, trans_b=bool(tb))
+    for name, sc, k, lg in topk:
+        sc = np.ascontiguousarray(sc, np.float32)
+        idx, val = ref.topk(sc, k, largest=bool(lg))
+        out[name + "__scores"], out[name + "__k"], out[name + "__largest"] = sc, np.array(k), np.array(lg)
+        out[name + "__idx"], out[name + "__val"] = idx, val
+    for name, src, ix in gather:
+        src = np.ascontiguousarray(src, np.float32)
+        out[name + "__src"], out[name + "__idx"] = src, ix.astype(np.int64)
+        out[name + "__out"] = ref.gather_rows(src, ix)
+    for name, xx, yy, m, arg in pairwise:
+        xx = np.ascontiguousarray(xx, np.float32)
+        yy = np.ascontiguousarray(yy, np.float32)
+        out[name + "__x"], out[name + "__y"] = xx, yy
+        out[name + "__metric"], out[name + "__arg"] = np.array(METRIC_IDS[m]), np.array(arg, np.float32)
+        out[name + "__out"] = ref.pairwise(METRIC_IDS[m], xx, yy, arg)
+    for name, data, m, k in allnb:
+        data = np.ascontiguousarray(data, np.float32)
+        nb, ds = ref.all_neighbors(data, k, METRIC_IDS[m])
+        out[name + "__data"], out[name + "__metric"], out[name + "__k"] = data, np.array(METRIC_IDS[m]), np.array(k)
+        out[name + "__neighbors"], out[name + "__distances"] = nb, ds
+    np.savez_compressed(os.path.join(OUT, "prims.npz"), **out)
+
+
 def main():
     ref = Reference()
     rng = np.random.default_rng(20261201)
@@ -171,6 +241,7 @@ def main():
                         topk_val=val, bitset_ids=np.array([2, 5, 9, 12, -1, 25, 19], np.int64),
                         bitset_n=np.array(20), bitset=bs,
                         version=np.array(ref.lib.ovvsGetVersion().decode()))
+    write_prims(ref, np.random.default_rng(20261202))
     print("wrote", sorted(f for f in os.listdir(OUT) if f.endswith(".npz")))
 
 

@@ -97,6 +97,57 @@ def test_argument_validation_order(ovvs):
     assert L.ovvsKMeansPredict(res._h, None, xp, 4, ctypes.c_void_p(nb.ctypes.data), None) == 2
 
 
+def test_primitive_argument_validation(ovvs):
+    """resources.cpp:178-216 and graphs.cpp:3384: null pointers or non-positive sizes ->
+    INVALID_ARGUMENT before any device work; with valid arguments and no GPU,
+    DEVICE_UNAVAILABLE (no CPU fallback)."""
+    import torch
+
+    L = ovvs.lib()
+    res = ovvs.Resources()
+    x = np.ones((8, 4), np.float32)
+    xp = ctypes.c_void_p(x.ctypes.data)
+    ip = ctypes.c_void_p(np.zeros(64, np.int64).ctypes.data)
+    i64 = ctypes.c_int64
+    gemm = [res._h, xp, xp, xp, i64(2), i64(2), i64(2), 1]
+    for i, bad in [(0, None), (1, None), (2, None), (3, None), (4, i64(0)), (5, i64(-1)),
+                   (6, i64(0))]:
+        a = list(gemm)
+        a[i] = bad
+        assert L.ovvsGemm(*a) == 2, i
+        assert L.ovvsGemmEx(*a, 1) == 2, i
+    topk = [res._h, xp, i64(2), i64(4), i64(2), ip, xp, 0]
+    for i, bad in [(0, None), (1, None), (2, i64(0)), (3, i64(0)), (4, i64(0)), (5, None),
+                   (6, None)]:
+        a = list(topk)
+        a[i] = bad
+        assert L.ovvsTopk(*a) == 2, i
+        assert L.ovvsKSelection(*a) == 2, i
+    gather = [res._h, xp, i64(8), i64(4), ip, i64(2), xp]
+    for i, bad in [(0, None), (1, None), (2, i64(0)), (3, i64(0)), (4, None), (5, i64(0)),
+                   (6, None)]:
+        a = list(gather)
+        a[i] = bad
+        assert L.ovvsGatherRows(*a) == 2, i
+    pw = [res._h, 0, xp, i64(2), xp, i64(2), i64(4), xp, ctypes.c_float(2.0)]
+    for i, bad in [(0, None), (2, None), (3, i64(0)), (4, None), (5, i64(0)), (6, i64(0)),
+                   (7, None)]:
+        a = list(pw)
+        a[i] = bad
+        assert L.ovvsPairwiseDistance(*a) == 2, i
+    an = [res._h, xp, i64(8), i64(4), 0, 2, ip, xp]
+    for i, bad in [(0, None), (1, None), (2, i64(1)), (5, 0), (6, None), (7, None)]:
+        a = list(an)
+        a[i] = bad
+        assert L.ovvsAllNeighbors(*a) == 2, i
+    if not torch.cuda.is_available():
+        assert L.ovvsGemm(*gemm) == 7
+        assert L.ovvsTopk(*topk) == 7
+        assert L.ovvsGatherRows(*gather) == 7
+        assert L.ovvsPairwiseDistance(*pw) == 7
+        assert L.ovvsAllNeighbors(*an) == 7
+
+
 def test_forced_cpu_or_npu_never_falls_back(ovvs):
     """FORCE_CPU / FORCE_NPU cannot be honoured by a GPU-only library: DEVICE_UNAVAILABLE
     (reference mixer.cpp:47-50: a forced device never falls back)."""
@@ -118,7 +169,6 @@ def test_out_of_scope_entry_points_are_unsupported(ovvs):
     L.ovvsIvfFlatBuild.restype = ctypes.c_int
     assert L.ovvsIvfFlatBuild(res._h, xp, ctypes.c_int64(8), ctypes.c_int64(4), 0, 2, ctypes.byref(h)) == 3
     assert L.ovvsCagraBuild(res._h, xp, ctypes.c_int64(8), ctypes.c_int64(4), 0, 4, 8, ctypes.byref(h)) == 3
-    assert L.ovvsGemm(res._h, xp, xp, xp, ctypes.c_int64(2), ctypes.c_int64(2), ctypes.c_int64(2), 1) == 3
     assert L.ovvsIvfFlatDestroy(None) == 0
     assert L.ovvsSyclEnabled() == 0
     assert L.ovvsGpuHasXmx() == -1

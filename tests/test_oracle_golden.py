@@ -74,3 +74,37 @@ def test_reference_library_matches_oracle(oracle, metric):
     a = oracle.brute_search(X, Q, 12, metric)
     b = ref.brute_search(X, Q, 12, metric)
     assert_search_equal(a[0], a[1], b[0], b[1], what=metric)
+
+
+def _gemm_shape(c):
+    m, k = c["a"].shape
+    n = c["b"].shape[0] if int(c["trans_b"]) else c["b"].shape[1]
+    return m, n, k
+
+
+def test_primitive_cases_bit_exact(golden_prims, oracle):
+    """resources.cpp:178-216 and graphs.cpp:3384-3396: the oracle's gemm / top-k / gather /
+    pairwise / all-neighbors equal the reference's outputs bit for bit."""
+    kinds = set()
+    for name, c in golden_prims.items():
+        kind = name.split("_", 1)[0]
+        kinds.add(kind)
+        if kind == "gemm":
+            m, n, k = _gemm_shape(c)
+            got = oracle.gemm(c["a"], c["b"], m, n, k, trans_b=bool(int(c["trans_b"])))
+            assert np.all(same_bits(got, c["c"])), name
+        elif kind == "topk":
+            idx, val = oracle.topk(c["scores"], int(c["k"]), largest=bool(int(c["largest"])))
+            assert np.array_equal(idx, c["idx"]), name
+            assert np.all(same_bits(val, c["val"])), name
+        elif kind == "gather":
+            assert np.all(same_bits(oracle.gather_rows(c["src"], c["idx"]), c["out"])), name
+        elif kind == "pw":
+            got = oracle.pairwise(int(c["metric"]), c["x"], c["y"], float(c["arg"]))
+            assert np.all(same_bits(got, c["out"])), name
+        elif kind == "an":
+            nb, ds = oracle.all_neighbors(c["data"], int(c["k"]), int(c["metric"]))
+            assert_search_equal(nb, ds, c["neighbors"], c["distances"], what=name)
+        else:
+            raise AssertionError(name)
+    assert kinds == {"gemm", "topk", "gather", "pw", "an"}
