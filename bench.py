@@ -48,6 +48,17 @@ CONFIGS = {
                 desc="L2 fp16, N=2M x 128 Gaussian mixture (1024 centres), Q=10k, k=10"),
     "c5": dict(metric="inner_product", dtype="f16", n=100_000_000, dim=96, nq=100_000, k=100,
                dist="unit", seed=4, desc="IP fp16, N=100M x 96 unit-norm, Q=100k, k=100"),
+    # profiling case: config 4's distribution with 500k rows (256 MB, > L2)
+    "c4s": dict(kind="kmeans", metric="l2", dtype="f32", n=500_000, dim=128, clusters=4096,
+                iters=10, dist="mixture", centres=4096, centre_std=3.0, seed=3,
+                desc="k-means fp32, N=500k x 128 Gaussian mixture (4096 centres), C=4096, "
+                     "10 iterations"),
+    # IVF-Flat (ovvsIvfFlatSearch), the next caller of the k-means path: one step = one search
+    # of all queries over a built index
+    "ivf": dict(kind="ivf", metric="l2", dtype="f32", n=1_000_000, dim=128, nq=10_000, k=10,
+                nlist=1024, nprobe=32, dist="mixture", centres=1024, centre_std=2.0, seed=5,
+                desc="IVF-Flat L2 fp32, N=1M x 128 Gaussian mixture (1024 centres, var 4), "
+                     "nlist=1024, nprobe=32, Q=10k, k=10"),
     # k-means (ovvsKMeansFit): one step = one full fit of `iters` Lloyd iterations
     "c4": dict(kind="kmeans", metric="l2", dtype="f32", n=5_000_000, dim=128, clusters=4096,
                iters=10, dist="mixture", centres=4096, centre_std=3.0, seed=3,
@@ -55,6 +66,7 @@ CONFIGS = {
                     "C=4096, 10 iterations"),
 }
 KMEANS_METRIC = "k-means Lloyd iterations/sec @ N=5M D=128 C=4096 fp32; % of roofline"
+IVF_METRIC = "IVF-Flat queries/sec @ N=1M D=128 fp32 L2 nlist=1024 nprobe=32 k=10"
 METRIC_NAME = "kNN queries/sec @ N=10M D=128 fp16 k=10 at 1/2/4/8 B200; % of roofline"
 
 
@@ -619,6 +631,259 @@ def run_kmeans(args, cfg):
     return 0
 
 
+def _ivf_reference_search(path, q_host, cfg, threads, nq_s):
+    """Times the reference's FORCE_CPU ovvsIvfFlatSearch over the index file `path` (the
+    reference's own format, read by its own ovvsIvfFlatDeserialize) on the first nq_s queries,
+    split over `threads` host threads, one Resources each (concurrent searches of one index are
+    allowed). Returns seconds."""
+    import ctypes
+
+    from oracle.cpu import Reference
+
+    ref = Reference()
+    L = ref.lib
+    L.ovvsIvfFlatDeserialize.argtypes = [ctypes.c_void_p, ctypes.c_char_p,
+                                         ctypes.POINTER(ctypes.c_void_p)]
+    L.ovvsIvfFlatSearch.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                    ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
+                                    ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    L.ovvsIvfFlatDestroy.argtypes = [ctypes.c_void_p]
+    res = [ref.resources() for _ in range(threads)]
+    ix = ctypes.c_void_p()
+    assert L.ovvsIvfFlatDeserialize(res[0], path.encode(), ctypes.byref(ix)) == 0
+    k = cfg["k"]
+    parts = np.array_split(np.arange(nq_s), threads)
+
+    def work(t):
+        idx = parts[t]
+        if idx.size == 0:
+            return
+        qq = np.ascontiguousarray(q_host[idx], np.float32)
+        nb = np.empty(idx.size * k, np.int64)
+        ds = np.empty(idx.size * k, np.float32)
+        assert L.ovvsIvfFlatSearch(res[t], ix, qq.ctypes.data, idx.size, k, cfg["nprobe"], None,
+                                   nb.ctypes.data, ds.ctypes.data) == 0
+
+    th = [threading.Thread(target=work, args=(t,)) for t in range(threads)]
+    t0 = time.perf_counter()
+    for x in th:
+        x.start()
+    for x in th:
+        x.join()
+    secs = time.perf_counter() - t0
+    L.ovvsIvfFlatDestroy(ix)
+    for r in res:
+        L.ovvsResourcesDestroy(r)
+    return secs
+
+
+def _ivf_file_lists(path):
+    """Centroids and list sizes from an IVF1 file (header: magic, version, n, dim, nlist,
+    metric; centroids; rows; per list an int32 size and its int64 ids)."""
+    with open(path, "rb") as f:
+        head = f.read(32)
+        n, dim = (int(v) for v in np.frombuffer(head[8:24], np.int64))
+        nlist = int(np.frombuffer(head[24:28], np.int32)[0])
+        cents = np.frombuffer(f.read(4 * nlist * dim), np.float32).reshape(nlist, dim)
+        f.seek(4 * n * dim, os.SEEK_CUR)
+        sizes = np.empty(nlist, np.int64)
+        for c in range(nlist):
+            sizes[c] = max(0, int(np.frombuffer(f.read(4), np.int32)[0]))
+            f.seek(8 * int(sizes[c]), os.SEEK_CUR)
+    return cents, sizes
+
+
+def _ivf_reference_sizes(cfg, seconds):
+    threads = max(1, min(os.cpu_count() or 1, 64))
+    per_query = cfg["dim"] * (cfg["nlist"] + cfg["n"] * cfg["nprobe"] / cfg["nlist"])
+    nq = int(seconds * 1.0e9 * threads / per_query)
+    return threads, max(threads, min(cfg["nq"], nq // threads * threads))
+
+
+def _ivf_setup(cfg, dev, torch, ov, res):
+    """Data, queries and the built index (timed) for the IVF config."""
+    data = _gen_rows(cfg, 0, cfg["n"], dev, torch)
+    data_host = data.cpu().numpy()
+    del data
+    t0 = time.perf_counter()
+    ix = ov.IvfFlatIndex.build(data_host, cfg["nlist"], cfg["metric"], resources=res)
+    build_s = time.perf_counter() - t0
+    dq = _queries(cfg, dev, torch)
+    return ix, build_s, dq, dq.cpu().numpy()
+
+
+def run_ivf(args, cfg):
+    """IVF-Flat arm (one GPU; with --gpus N each rank is an independent replica searching the
+    same queries, no collective). `value` = device-resident searches (ovvsIvfFlatSearchDevice),
+    `e2e` = host-buffer searches through ovvsIvfFlatSearch. Roofline: the list scan kernel, whose
+    exact sequential fp32 sums run on the CUDA cores (two dependent instructions per MAC), against
+    the FP32 issue rate of the SMs at the sampled clock."""
+    import tempfile
+
+    import torch
+    import torch.distributed as dist
+
+    import ovvs_b200 as ov
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    res = ov.Resources.sharded(local, 0, 1, None)
+    nq, k, dim = cfg["nq"], cfg["k"], cfg["dim"]
+    ix, build_s, dq, q_host = _ivf_setup(cfg, dev, torch, ov, res)
+    dn = torch.empty((nq, k), dtype=torch.int64, device=dev)
+    dd = torch.empty((nq, k), dtype=torch.float32, device=dev)
+    stream = torch.cuda.ExternalStream(res.stream(), device=dev)
+    for _ in range(args.warmup):
+        ix.search_device(dq, k, cfg["nprobe"], dn, dd)
+    res.synchronize()
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    res.set_profiling(True)
+    phases = []
+    barrier()
+    with ClockSampler(local) as clocks:
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            ix.search_device(dq, k, cfg["nprobe"], dn, dd)
+            phases.append(res.last_phase_ms())
+        ev1.record(stream)
+        ev1.synchronize()
+        barrier()
+    res.set_profiling(False)
+    ms_step = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
+    nb_h, ds_h = ix.search(q_host, k, cfg["nprobe"])
+    barrier()
+    e0 = time.perf_counter()
+    for _ in range(args.steps):
+        nb_h, ds_h = ix.search(q_host, k, cfg["nprobe"])
+    e2e_ms = max_over_ranks((time.perf_counter() - e0) * 1e3 / args.steps)
+    assert np.array_equal(nb_h, dn.cpu().numpy())
+    scan_ms = statistics.mean(p[1] for p in phases)
+    clk = clocks.summary()
+    # candidates actually scored: the probed lists' sizes per query
+    path = os.path.join(tempfile.mkdtemp(), "ivf.bin")
+    ix.save(path)
+    cents, sizes = _ivf_file_lists(path)
+    cn = (cents ** 2).sum(1)
+    qs = q_host[:2000]
+    d = (qs ** 2).sum(1)[:, None] + cn[None, :] - 2 * qs @ cents.T
+    probes = np.argsort(d, axis=1, kind="stable")[:, :cfg["nprobe"]]
+    cand_mean = float(sizes[probes].sum(1).mean())
+    macs = nq * cand_mean * dim
+    sm_mhz = clk["sm_mhz"] or 1965.0
+    # FP32 lanes per SM x SMs x clock: one separately rounded multiply and one add per MAC
+    fp32_gops = 128 * torch.cuda.get_device_properties(dev).multi_processor_count * sm_mhz / 1e3
+    achieved = 2 * macs / (scan_ms / 1e3) / 1e12
+    peak = fp32_gops / 1e3
+    ix.close()
+    res.close()
+    line = None
+    if rank == 0:
+        line = {
+            "metric": IVF_METRIC, "value": world * nq / (ms_step / 1e3), "unit": "queries/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": f"{args.config}: {cfg['desc']}", "n": cfg["n"], "dim": dim,
+                       "nq": nq, "k": k, "nlist": cfg["nlist"], "nprobe": cfg["nprobe"],
+                       "parallelism": "1 GPU" if world == 1 else
+                       f"{world} independent replicas (the IVF path is not sharded)",
+                       "l2": "inputs larger than L2 (rows 512 MB >> 126 MB), no flush needed",
+                       "build_s": round(build_s, 3), "candidates_per_query": round(cand_mean, 1),
+                       "phase_ms_mean": [round(statistics.mean(p[i] for p in phases), 4)
+                                         for i in range(4)]},
+            "e2e": {"value": world * nq / (e2e_ms / 1e3), "unit": "queries/s",
+                    "h2d_bytes_per_step": nq * dim * 4, "d2h_bytes_per_step": nq * k * 12},
+            "gpu_launches": 12 * args.steps,
+            "roofline": {"bound": "fp32", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": None, "kernel": "list_scan_kernel",
+                         "flops_per_launch": 2 * macs,
+                         "note": "exact sequential fp32 scores (separate multiply and add) on the "
+                                 "CUDA cores; peak = 128 FP32 lanes x SMs x median SM clock, one "
+                                 "instruction per flop"},
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"],
+                       "reasons": clk["reasons"]},
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            threads, nq_s = _ivf_reference_sizes(cfg, args.ref_seconds)
+            secs = _ivf_reference_search(path, q_host, cfg, threads, nq_s)
+            line["cpu_baseline"] = {
+                "value": nq_s / secs, "unit": "queries/s", "cores": threads, "kind": "reference",
+                "sample": f"{nq_s} of {nq} queries through the reference library built from its "
+                          f"sources (oracle/_ref), FORCE_CPU, {threads} threads, over this "
+                          "index written in the reference's IVF1 file format"}
+    os.remove(path)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ivf_reference(args, cfg):
+    """--impl reference for the IVF config: the reference's own ovvsIvfFlatDeserialize +
+    ovvsIvfFlatSearch (FORCE_CPU, all host threads) over an index file in its format. Building
+    the reference's index on the host (12 Lloyd iterations over 1M x 1024 x 128) would take
+    about half an hour, so the index is built on the GPU by this library and written in the
+    reference's file format; only the reference's search is timed."""
+    import tempfile
+
+    import torch
+
+    import ovvs_b200 as ov
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    res = ov.Resources.sharded(dev.index, 0, 1, None)
+    ix, _, _, q_host = _ivf_setup(cfg, dev, torch, ov, res)
+    path = os.path.join(tempfile.mkdtemp(), "ivf.bin")
+    ix.save(path)
+    ix.close()
+    res.close()
+    threads, nq_s = _ivf_reference_sizes(cfg, args.ref_seconds)
+    for _ in range(args.warmup):
+        _ivf_reference_search(path, q_host, cfg, threads, threads)
+    secs = [_ivf_reference_search(path, q_host, cfg, threads, nq_s) for _ in range(args.steps)]
+    os.remove(path)
+    value = nq_s * args.steps / sum(secs)
+    sample = (f"{nq_s} of {cfg['nq']} queries per step, FORCE_CPU, {threads} threads with one "
+              "Resources each, over an index in the reference's IVF1 file format")
+    print(json.dumps({
+        "metric": IVF_METRIC, "value": value, "unit": "queries/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(secs) / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": f"{args.config}: {cfg['desc']}", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "queries/s", "cores": threads,
+                         "kind": "reference", "sample": sample},
+        "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0}}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -635,9 +900,13 @@ def main():
         args.warmup = 3
     cfg = CONFIGS[args.config]
     if args.impl == "reference":
+        if cfg.get("kind") == "ivf":
+            return run_ivf_reference(args, cfg)
         return run_reference_arm(args, cfg)
     if cfg.get("kind") == "kmeans":
         return run_kmeans(args, cfg)
+    if cfg.get("kind") == "ivf":
+        return run_ivf(args, cfg)
     return run_ours(args, cfg)
 
 
