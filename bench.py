@@ -122,16 +122,69 @@ def _queries(cfg, device, torch):
 # clocks
 # ---------------------------------------------------------------------------------------------
 class ClockSampler:
+    """SM clock and clock-event reasons sampled DURING the timed region (read-only queries).
+
+    NVML is polled from a thread every ~2 ms, so even a timed region of a few milliseconds (a
+    sharded search on 8 GPUs) gets samples; the first sample is taken before __enter__ returns.
+    Without NVML it falls back to `nvidia-smi -lms 100` (and waits for its first line)."""
+
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits (nvmlClocksEventReason*)
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40}
 
     def __init__(self, device_index):
         self.dev = device_index
         self.proc = None
         self.lines = []
+        self.nvml = None
+        self._stop = threading.Event()
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        try:
+            p = torch.cuda.get_device_properties(self.dev)
+            bus = f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.dev)
+
+    def _poll(self):
+        nv, h = self.nvml
+        try:
+            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        except Exception:
+            mx = 0
+        while True:
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                fl = ["Active" if bits & self.REASON_BITS[n] else "Not Active"
+                      for n in ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                                "sw_power_cap")]
+                self.lines.append(", ".join([str(sm), str(mx), "0"] + fl))
+            except Exception:
+                pass
+            if self._stop.wait(0.002):
+                break
 
     def __enter__(self):
+        try:
+            self.nvml = self._nvml_handle()
+        except Exception:
+            self.nvml = None
+        if self.nvml is not None:
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            t0 = time.perf_counter()
+            while not self.lines and time.perf_counter() - t0 < 2.0:
+                time.sleep(0.001)
+            return self
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -139,6 +192,9 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.perf_counter()
+            while not self.lines and time.perf_counter() - t0 < 5.0:
+                time.sleep(0.01)
         except OSError:
             self.proc = None
         return self
@@ -148,6 +204,9 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        if self.nvml is not None:
+            self._stop.set()
+            self.t.join(timeout=5)
         if self.proc:
             self.proc.terminate()
             try:
