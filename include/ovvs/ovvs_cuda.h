@@ -88,6 +88,16 @@ OVVS_API ovvsStatus ovvsBruteForceSearchDeviceNoAlloc(ovvsResources_t res,
                                                       int64_t* d_neighbors, float* d_distances,
                                                       void* stream);
 
+/* Device-pointer IVF-Flat search: the contract of ovvsIvfFlatSearch (reference
+   src/neighbors/indexes.cpp:302-358; outputs [nq x k], -1 / +inf past a query's candidates) with
+   queries, bitset (indexed by row id, covering the index's rows), neighbors and distances in GPU
+   memory on the Resources' device. Only enqueues work on the Resources' stream; synchronise
+   before reading the results. Not in the reference. */
+OVVS_API ovvsStatus ovvsIvfFlatSearchDevice(ovvsResources_t res, ovvsIvfFlatIndex_t index,
+                                            const float* d_queries, int64_t nq, int64_t k,
+                                            int32_t nprobe, const uint8_t* d_bitset,
+                                            int64_t* d_neighbors, float* d_distances);
+
 /* ---- one process per GPU ------------------------------------------------------------------ */
 
 /* Size in bytes of the NCCL unique id that ovvsNcclUniqueId writes (128). */

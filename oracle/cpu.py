@@ -93,6 +93,15 @@ class Oracle:
         L.oracle_bitset_from_allow_list.argtypes = [c_int64, POINTER(c_int64), c_int64,
                                                     POINTER(c_uint8)]
         L.oracle_bitset_from_allow_list.restype = c_int32
+        L.oracle_ivf_flat_build.argtypes = [POINTER(c_float), c_int64, c_int64, c_int32,
+                                            POINTER(c_float), POINTER(c_int64), POINTER(c_int64),
+                                            c_int32]
+        L.oracle_ivf_flat_build.restype = c_int32
+        L.oracle_ivf_flat_search.argtypes = [POINTER(c_float), c_int64, c_int64, c_int32,
+                                             POINTER(c_float), c_int32, POINTER(c_int64),
+                                             POINTER(c_int64), POINTER(c_float), c_int64, c_int64,
+                                             c_int32, POINTER(c_uint8), POINTER(c_int64),
+                                             POINTER(c_float), c_int32]
         self.nthreads = max(1, os.cpu_count() or 1)
 
     # -- conversions ---------------------------------------------------------------------
@@ -206,6 +215,38 @@ class Oracle:
         keff = self.lib.oracle_kmeans_init_rows(n, k, _ptr(rows, c_int64))
         return rows[:keff]
 
+    def ivf_flat_build(self, x, nlist):
+        """(centroids [nlist_eff, dim], list sizes [nlist_eff], list ids concatenated [n])."""
+        x = _f32(x)
+        n, dim = x.shape
+        ne = max(1, min(nlist, n))
+        c = np.zeros((ne, dim), np.float32)
+        sizes = np.zeros(ne, np.int64)
+        ids = np.zeros(n, np.int64)
+        keff = self.lib.oracle_ivf_flat_build(_ptr(x, c_float), n, dim, nlist, _ptr(c, c_float),
+                                              _ptr(sizes, c_int64), _ptr(ids, c_int64),
+                                              self.nthreads)
+        if keff < 0:
+            raise ValueError("invalid IVF-Flat arguments")
+        return c[:keff], sizes[:keff], ids[: int(sizes[:keff].sum())]
+
+    def ivf_flat_search(self, x, metric, centroids, sizes, ids, queries, k, nprobe, bitset=None):
+        x, centroids, queries = _f32(x), _f32(centroids), _f32(queries)
+        sizes = np.ascontiguousarray(sizes, np.int64)
+        ids = np.ascontiguousarray(ids, np.int64)
+        m = METRICS[metric] if isinstance(metric, str) else int(metric)
+        nq = queries.shape[0]
+        nb = np.empty(nq * k, np.int64)
+        ds = np.empty(nq * k, np.float32)
+        bs = None if bitset is None else np.ascontiguousarray(bitset, np.uint8)
+        self.lib.oracle_ivf_flat_search(_ptr(x, c_float), x.shape[0], x.shape[1], m,
+                                        _ptr(centroids, c_float), centroids.shape[0],
+                                        _ptr(sizes, c_int64), _ptr(ids, c_int64),
+                                        _ptr(queries, c_float), nq, k, nprobe,
+                                        _ptr(bs, c_uint8) if bs is not None else None,
+                                        _ptr(nb, c_int64), _ptr(ds, c_float), self.nthreads)
+        return nb.reshape(nq, k), ds.reshape(nq, k)
+
     def bitset_from_allow_list(self, n, ids):
         ids = np.ascontiguousarray(ids, np.int64)
         bs = np.zeros((n + 7) // 8, np.uint8)
@@ -253,6 +294,44 @@ class Reference:
                                            c_float]
         L.ovvsAllNeighbors.argtypes = [c_void_p, POINTER(c_float), c_int64, c_int64, c_int32,
                                        c_int32, POINTER(c_int64), POINTER(c_float)]
+
+    def ivf_flat(self, x, nlist, metric, queries, k, nprobe, bitset=None, extra=None):
+        """Builds an IVF-Flat index with the reference (FORCE_CPU), optionally extends it with
+        `extra` rows, searches, and returns (neighbors [nq, k], distances [nq, k], the index as
+        written by the reference's ovvsIvfFlatSerialize: dict of centroids / sizes / ids)."""
+        import tempfile
+
+        L = self.lib
+        L.ovvsIvfFlatBuild.argtypes = [c_void_p, POINTER(c_float), c_int64, c_int64, c_int32,
+                                       c_int32, POINTER(c_void_p)]
+        L.ovvsIvfFlatSearch.argtypes = [c_void_p, c_void_p, POINTER(c_float), c_int64, c_int64,
+                                        c_int32, c_void_p, POINTER(c_int64), POINTER(c_float)]
+        L.ovvsIvfFlatSerialize.argtypes = [c_void_p, ctypes.c_char_p]
+        L.ovvsIvfFlatExtend.argtypes = [c_void_p, c_void_p, POINTER(c_float), c_int64]
+        L.ovvsIvfFlatDestroy.argtypes = [c_void_p]
+        x, queries = _f32(x), _f32(queries)
+        m = METRICS[metric] if isinstance(metric, str) else int(metric)
+        res = self.resources()
+        ix = c_void_p()
+        assert L.ovvsIvfFlatBuild(res, _ptr(x, c_float), x.shape[0], x.shape[1], m, nlist,
+                                  ctypes.byref(ix)) == 0
+        if extra is not None:
+            e = _f32(extra)
+            assert L.ovvsIvfFlatExtend(res, ix, _ptr(e, c_float), e.shape[0]) == 0
+        nq = queries.shape[0]
+        nb = np.empty(nq * k, np.int64)
+        ds = np.empty(nq * k, np.float32)
+        bs = None if bitset is None else np.ascontiguousarray(bitset, np.uint8)
+        assert L.ovvsIvfFlatSearch(res, ix, _ptr(queries, c_float), nq, k, nprobe,
+                                   bs.ctypes.data if bs is not None else None,
+                                   _ptr(nb, c_int64), _ptr(ds, c_float)) == 0
+        with tempfile.TemporaryDirectory() as d:
+            path = os.path.join(d, "ivf.bin")
+            assert L.ovvsIvfFlatSerialize(ix, path.encode()) == 0
+            parts = read_ivf1(path)
+        L.ovvsIvfFlatDestroy(ix)
+        L.ovvsResourcesDestroy(res)
+        return nb.reshape(nq, k), ds.reshape(nq, k), parts
 
     def resources(self):
         r = c_void_p()
@@ -388,3 +467,44 @@ def make_data(n: int, dim: int, seed: int) -> np.ndarray:
     # C++: (static_cast<int>(s >> 16) % 2000) / 1000.f - 1.f
     out[:] = (vals % 2000).astype(np.float32) / np.float32(1000.0) - np.float32(1.0)
     return out.reshape(n, dim)
+
+
+def read_ivf1(path):
+    """Parses an index file in the reference's IVF1 format (indexes.cpp:368-394): magic, version,
+    n, dim, nlist, metric, centroids, rows, then per list an int32 size and its int64 ids."""
+    with open(path, "rb") as f:
+        buf = f.read()
+    n, dim = (int(v) for v in np.frombuffer(buf[8:24], np.int64))
+    nlist, metric = (int(v) for v in np.frombuffer(buf[24:32], np.int32))
+    at = 32
+    cents = np.frombuffer(buf[at: at + 4 * nlist * dim], np.float32).reshape(nlist, dim).copy()
+    at += 4 * nlist * dim
+    x = np.frombuffer(buf[at: at + 4 * n * dim], np.float32).reshape(n, dim).copy()
+    at += 4 * n * dim
+    sizes, ids = [], []
+    for _ in range(nlist):
+        sz = max(0, int(np.frombuffer(buf[at: at + 4], np.int32)[0]))
+        at += 4
+        sizes.append(sz)
+        ids.append(np.frombuffer(buf[at: at + 8 * sz], np.int64))
+        at += 8 * sz
+    return {"n": n, "dim": dim, "nlist": nlist, "metric": metric, "centroids": cents, "x": x,
+            "sizes": np.array(sizes, np.int64),
+            "ids": np.concatenate(ids) if ids else np.zeros(0, np.int64)}
+
+
+def write_ivf1(path, x, centroids, sizes, ids, metric):
+    """Writes an index in the reference's IVF1 format (the inverse of read_ivf1)."""
+    x = np.ascontiguousarray(x, np.float32)
+    centroids = np.ascontiguousarray(centroids, np.float32).reshape(-1, x.shape[1])
+    with open(path, "wb") as f:
+        f.write(np.array([0x31465649, 1], np.uint32).tobytes())
+        f.write(np.array([x.shape[0], x.shape[1]], np.int64).tobytes())
+        f.write(np.array([centroids.shape[0], metric], np.int32).tobytes())
+        f.write(centroids.tobytes())
+        f.write(x.tobytes())
+        at = 0
+        for sz in np.asarray(sizes, np.int64):
+            f.write(np.array([sz], np.int32).tobytes())
+            f.write(np.ascontiguousarray(ids[at: at + sz], np.int64).tobytes())
+            at += int(sz)

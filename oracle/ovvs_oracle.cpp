@@ -414,4 +414,99 @@ int32_t oracle_bitset_from_allow_list(int64_t n, const int64_t* ids, int64_t nid
   return 0;
 }
 
+/* indexes.cpp:281-300 ovvsIvfFlatBuild + build_ivf_lists (indexes.cpp:50-57). */
+int32_t oracle_ivf_flat_build(const float* x, int64_t n, int64_t dim, int32_t nlist,
+                              float* centroids, int64_t* list_sizes, int64_t* list_ids,
+                              int32_t nthreads) {
+  if (!x || n <= 0 || dim <= 0 || nlist <= 0) return -1;
+  nlist = static_cast<int32_t>(std::min<int64_t>(nlist, n));
+  const int32_t keff = oracle_kmeans_fit(x, n, dim, nlist, 12, centroids, nthreads);
+  if (keff < 0) return -1;
+  std::vector<int64_t> labels(static_cast<size_t>(n));
+  oracle_kmeans_predict(centroids, keff, dim, x, n, labels.data(), nullptr, nthreads);
+  std::vector<std::vector<int64_t>> lists(static_cast<size_t>(keff));
+  for (int64_t i = 0; i < n; ++i) {
+    const int64_t a = labels[static_cast<size_t>(i)];
+    if (a >= 0 && a < keff) lists[static_cast<size_t>(a)].push_back(i);
+  }
+  int64_t at = 0;
+  for (int32_t c = 0; c < keff; ++c) {
+    list_sizes[c] = static_cast<int64_t>(lists[static_cast<size_t>(c)].size());
+    for (int64_t id : lists[static_cast<size_t>(c)]) list_ids[at++] = id;
+  }
+  return keff;
+}
+
+/* indexes.cpp:302-358 ovvsIvfFlatSearch over an index given by its parts (the dataset in row
+   order, centroids, and the lists concatenated with their sizes). Filtered rows score +inf; a
+   list id outside [0, n) is gathered as a zero row (cpu_gather_rows) and counts as filtered when
+   a bitset is given (the reference would read past the bitset). */
+void oracle_ivf_flat_search(const float* x, int64_t n, int64_t dim, int32_t metric,
+                            const float* centroids, int32_t nlist, const int64_t* list_sizes,
+                            const int64_t* list_ids, const float* queries, int64_t nq, int64_t k,
+                            int32_t nprobe, const uint8_t* bitset, int64_t* neighbors,
+                            float* distances, int32_t nthreads) {
+  const float inf = std::numeric_limits<float>::infinity();
+  std::vector<int64_t> off(static_cast<size_t>(nlist) + 1, 0);
+  for (int32_t c = 0; c < nlist; ++c) off[c + 1] = off[c] + list_sizes[c];
+  std::vector<float> cnorm(static_cast<size_t>(nlist));
+  for (int32_t c = 0; c < nlist; ++c) cnorm[static_cast<size_t>(c)] = nrm2sq_seq(centroids + c * dim, dim);
+  nprobe = std::max(1, std::min(nprobe, nlist));
+  parallel_for(nq, nthreads, [&](int64_t q0, int64_t q1) {
+    std::vector<float> cs(static_cast<size_t>(nlist));
+    std::vector<int64_t> cl(static_cast<size_t>(nprobe));
+    std::vector<float> cd(static_cast<size_t>(nprobe));
+    for (int64_t q = q0; q < q1; ++q) {
+      const float* qr = queries + q * dim;
+      std::vector<int64_t> ids;
+      if (nlist > 0) {
+        pairwise_block(kL2, qr, 1, centroids, nlist, dim, cnorm.data(), cs.data(), 2.f);
+        topk_rows(cs.data(), 1, nlist, nprobe, cl.data(), cd.data(), false);
+        for (int32_t p = 0; p < nprobe; ++p) {
+          const int64_t c = cl[static_cast<size_t>(p)];
+          if (c < 0 || c >= nlist) continue;
+          ids.insert(ids.end(), list_ids + off[c], list_ids + off[c + 1]);
+        }
+      }
+      if (ids.empty()) {
+        for (int64_t t = 0; t < k; ++t) {
+          neighbors[q * k + t] = -1;
+          distances[q * k + t] = inf;
+        }
+        continue;
+      }
+      const int64_t m = static_cast<int64_t>(ids.size());
+      std::vector<float> g(static_cast<size_t>(m * dim));
+      oracle_gather_rows(x, n, dim, ids.data(), m, g.data());
+      std::vector<float> gn(static_cast<size_t>(m));
+      for (int64_t j = 0; j < m; ++j) gn[static_cast<size_t>(j)] = nrm2sq_seq(g.data() + j * dim, dim);
+      std::vector<float> sc(static_cast<size_t>(m));
+      pairwise_block(metric, qr, 1, g.data(), m, dim, gn.data(), sc.data(), 2.f);
+      if (bitset) {
+        for (int64_t j = 0; j < m; ++j) {
+          const int64_t id = ids[static_cast<size_t>(j)];
+          const bool ok = id >= 0 && id < n && ((bitset[id >> 3] >> (id & 7)) & 1);
+          if (!ok) sc[static_cast<size_t>(j)] = inf;
+        }
+      }
+      const int64_t kk = std::min(k, m);
+      std::vector<int64_t> ti(static_cast<size_t>(kk));
+      std::vector<float> tv(static_cast<size_t>(kk));
+      topk_rows(sc.data(), 1, m, kk, ti.data(), tv.data(), false);
+      for (int64_t t = 0; t < k; ++t) {
+        if (t < kk) {
+          neighbors[q * k + t] = ids[static_cast<size_t>(ti[static_cast<size_t>(t)])];
+          float d = tv[static_cast<size_t>(t)];
+          if (metric == kIP) d = -d;
+          distances[q * k + t] = d;
+        } else {
+          neighbors[q * k + t] = -1;
+          distances[q * k + t] = inf;
+        }
+      }
+    }
+  });
+}
+
 }  // extern "C"
+

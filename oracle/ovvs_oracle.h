@@ -75,6 +75,20 @@ int32_t oracle_kmeans_init_rows(int64_t n, int32_t k, int64_t* rows);
 int32_t oracle_bitset_from_allow_list(int64_t n, const int64_t* ids, int64_t nids,
                                       uint8_t* bitset);
 
+/* indexes.cpp:281-300 ovvsIvfFlatBuild: nlist_eff = min(nlist, n) centroids (12 Lloyd
+   iterations), list_sizes [nlist_eff] and list_ids [n] (the lists concatenated, ascending ids).
+   Returns nlist_eff, or -1 for invalid arguments. */
+int32_t oracle_ivf_flat_build(const float* x, int64_t n, int64_t dim, int32_t nlist,
+                              float* centroids, int64_t* list_sizes, int64_t* list_ids,
+                              int32_t nthreads);
+
+/* indexes.cpp:302-358 ovvsIvfFlatSearch over an index given by its parts; outputs [nq x k]. */
+void oracle_ivf_flat_search(const float* x, int64_t n, int64_t dim, int32_t metric,
+                            const float* centroids, int32_t nlist, const int64_t* list_sizes,
+                            const int64_t* list_ids, const float* queries, int64_t nq, int64_t k,
+                            int32_t nprobe, const uint8_t* bitset, int64_t* neighbors,
+                            float* distances, int32_t nthreads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -19,7 +19,7 @@ from ctypes import POINTER, byref, c_char_p, c_float, c_int32, c_int64, c_uint8,
 import numpy as np
 
 __all__ = [
-    "OvvsError", "Resources", "BruteIndex", "KMeans", "Batcher", "neighbors",
+    "OvvsError", "Resources", "BruteIndex", "IvfFlatIndex", "KMeans", "Batcher", "neighbors",
     "bitset_from_allow_list", "version", "library_path", "nccl_unique_id",
     "METRIC", "DTYPE", "POLICY", "STATUS",
 ]
@@ -94,7 +94,17 @@ def _bind(lib):
                                   c_int64, c_void_p, c_float], c_int32),
         "ovvsAllNeighbors": ([c_void_p, c_void_p, c_int64, c_int64, c_int32, c_int32, c_void_p,
                               c_void_p], c_int32),
+        "ovvsIvfFlatBuild": ([c_void_p, c_void_p, c_int64, c_int64, c_int32, c_int32,
+                              P(c_void_p)], c_int32),
+        "ovvsIvfFlatSearch": ([c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int32, c_void_p,
+                               c_void_p, c_void_p], c_int32),
+        "ovvsIvfFlatSerialize": ([c_void_p, c_char_p], c_int32),
+        "ovvsIvfFlatDeserialize": ([c_void_p, c_char_p, P(c_void_p)], c_int32),
+        "ovvsIvfFlatExtend": ([c_void_p, c_void_p, c_void_p, c_int64], c_int32),
+        "ovvsIvfFlatDestroy": ([c_void_p], c_int32),
         # extensions (include/ovvs/ovvs_cuda.h)
+        "ovvsIvfFlatSearchDevice": ([c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int32,
+                                     c_void_p, c_void_p, c_void_p], c_int32),
         "ovvsResourcesStream": ([c_void_p, P(c_void_p)], c_int32),
         "ovvsResourcesSynchronize": ([c_void_p], c_int32),
         "ovvsResourcesDevice": ([c_void_p, P(c_int32)], c_int32),
@@ -426,6 +436,79 @@ class BruteIndex:
                                                        _dev_ptr(neighbors), _dev_ptr(distances),
                                                        c_void_p(int(stream))),
                "device search without allocation")
+
+
+class IvfFlatIndex:
+    """IVF-Flat index (ovvsIvfFlat*): k-means lists (12 Lloyd iterations, squared-L2 coarse
+    assignment) scanned exactly with the index metric. Results are [nq, k] arrays, -1 / +inf past
+    a query's candidates (indexes.cpp:302-358)."""
+
+    def __init__(self, res: Resources, handle: c_void_p, dim: int, own_res: bool = False):
+        self._res, self._h, self.dim, self._own = res, handle, dim, own_res
+
+    @classmethod
+    def build(cls, dataset, nlist=16, metric="l2", resources: Resources | None = None):
+        res = resources or Resources()
+        a = np.ascontiguousarray(np.asarray(dataset, dtype=np.float32))
+        m = METRIC[metric] if isinstance(metric, str) else int(metric)
+        h = c_void_p()
+        _check(lib().ovvsIvfFlatBuild(res._h, _ptr(a), a.shape[0], a.shape[1], m, int(nlist),
+                                      byref(h)), "ivf-flat build")
+        return cls(res, h, a.shape[1], own_res=resources is None)
+
+    @classmethod
+    def load(cls, path, dim=None, resources: Resources | None = None):
+        """Reads an index file in the reference's IVF1 format (ovvsIvfFlatDeserialize)."""
+        res = resources or Resources()
+        h = c_void_p()
+        _check(lib().ovvsIvfFlatDeserialize(res._h, os.fsencode(path), byref(h)),
+               "ivf-flat deserialize")
+        if dim is None:
+            with open(path, "rb") as f:
+                dim = int(np.frombuffer(f.read(24)[16:24], np.int64)[0])
+        return cls(res, h, dim, own_res=resources is None)
+
+    def save(self, path):
+        _check(lib().ovvsIvfFlatSerialize(self._h, os.fsencode(path)), "ivf-flat serialize")
+
+    def extend(self, rows):
+        a = np.ascontiguousarray(np.asarray(rows, dtype=np.float32).reshape(-1, self.dim))
+        _check(lib().ovvsIvfFlatExtend(self._res._h, self._h, _ptr(a), a.shape[0]),
+               "ivf-flat extend")
+
+    def search(self, queries, k=10, nprobe=1, bitset=None, allow_list=None, n=None):
+        q = np.ascontiguousarray(np.asarray(queries, dtype=np.float32).reshape(-1, self.dim))
+        nq = q.shape[0]
+        if allow_list is not None:
+            bitset = bitset_from_allow_list(int(n), allow_list)
+        bs = None if bitset is None else np.ascontiguousarray(bitset, dtype=np.uint8)
+        nb = np.full(nq * k, -1, np.int64)
+        ds = np.zeros(nq * k, np.float32)
+        _check(lib().ovvsIvfFlatSearch(self._res._h, self._h, _ptr(q), nq, k, int(nprobe),
+                                       _ptr(bs), _ptr(nb), _ptr(ds)), "ivf-flat search")
+        return nb.reshape(nq, k), ds.reshape(nq, k)
+
+    def search_device(self, queries, k, nprobe, neighbors, distances, bitset=None):
+        """Enqueue a search on device buffers: queries [nq, dim] f32, neighbors [nq, k] i64,
+        distances [nq, k] f32 (objects with data_ptr(), e.g. CUDA torch tensors)."""
+        nq = int(queries.shape[0])
+        _check(lib().ovvsIvfFlatSearchDevice(self._res._h, self._h, _dev_ptr(queries), nq, k,
+                                             int(nprobe), _dev_ptr(bitset), _dev_ptr(neighbors),
+                                             _dev_ptr(distances)), "ivf-flat device search")
+
+    def close(self):
+        if self._h:
+            lib().ovvsIvfFlatDestroy(self._h)
+            self._h = c_void_p()
+        if self._own and self._res:
+            self._res.close()
+            self._res = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class neighbors:  # noqa: N801  (mirrors the reference's namespace class)

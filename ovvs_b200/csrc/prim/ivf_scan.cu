@@ -1,0 +1,584 @@
+// IVF-Flat list scan kernels (see ivf_scan.cuh).
+#include "ivf_scan.cuh"
+
+#include <math.h>
+
+#include "keys.cuh"
+
+namespace ovvs {
+namespace prim {
+namespace {
+
+constexpr int kThreads = 256;  // 16 x 16 threads, 4 x 4 (pair, row) scores each (strided by 16)
+constexpr int kTK = 16;        // K slab staged in shared memory
+constexpr int kPadP = kIvfPairs + 1;
+constexpr int kPadR = kIvfRows + 1;
+
+// ovvsMetric values (ovvs.h)
+constexpr int kRawL2 = 0, kRawL2Sqrt = 1, kRawIp = 2, kRawCosine = 3, kRawHamming = 4, kRawLp = 5;
+
+// How a metric accumulates over the dimensions (prim_pairwise, mixer.cpp:174-197: the three
+// expanded metrics go through the dot product; every other one through distance_one,
+// internal.hpp:240-272, whose default is the squared L2 of l2sq).
+enum AccKind : int { kAccDot = 0, kAccL2 = 1, kAccHamming = 2, kAccLp = 3 };
+
+__host__ __device__ inline int acc_kind(int metric) {
+  switch (metric) {
+    case kRawL2:
+    case kRawIp:
+    case kRawCosine:
+      return kAccDot;
+    case kRawHamming:
+      return kAccHamming;
+    case kRawLp:
+      return kAccLp;
+    default:
+      return kAccL2;
+  }
+}
+
+// The IVF search calls prim_pairwise with metric_arg = 2 (indexes.cpp:334).
+constexpr float kLpP = 2.f;
+
+template <int ACC>
+__device__ __forceinline__ void accumulate(float& acc, int& cnt, float x, float y) {
+  if constexpr (ACC == kAccDot) {
+    acc = __fadd_rn(acc, __fmul_rn(x, y));
+  } else if constexpr (ACC == kAccL2) {
+    const float d = __fsub_rn(x, y);
+    acc = __fadd_rn(acc, __fmul_rn(d, d));
+  } else if constexpr (ACC == kAccHamming) {
+    cnt += static_cast<int>((x >= 0.f) != (y >= 0.f));
+  } else {
+    const float p = kLpP;
+    acc = __fadd_rn(acc, powf(fabsf(__fsub_rn(x, y)), p));
+  }
+}
+
+// The score of one (query, row) pair from its accumulated value: the reference's epilogue
+// (mixer.cpp:184-197) for the expanded metrics, distance_one's last step for the others.
+template <int ACC>
+__device__ __forceinline__ float finish(int metric, float acc, int cnt, float qn, float yn) {
+  if constexpr (ACC == kAccDot) {
+    if (metric == kRawIp) return -acc;
+    if (metric == kRawCosine) {
+      const float nxv = __fsqrt_rn(qn < 1e-12f ? 1e-12f : qn);
+      const float nyv = __fsqrt_rn(yn < 1e-12f ? 1e-12f : yn);
+      return __fsub_rn(1.f, __fdiv_rn(acc, __fmul_rn(nxv, nyv)));
+    }
+    return __fsub_rn(__fadd_rn(qn, yn), __fmul_rn(2.f, acc));
+  } else if constexpr (ACC == kAccL2) {
+    return metric == kRawL2Sqrt ? __fsqrt_rn(acc) : acc;
+  } else if constexpr (ACC == kAccHamming) {
+    return static_cast<float>(cnt);
+  } else {
+    const float p = kLpP;
+    return powf(acc, __fdiv_rn(1.f, p));
+  }
+}
+
+// allowed() of internal.hpp:274-277. Ids outside the dataset occur only in a hand-made index
+// file; the reference would read past the bitset for them, here they count as filtered.
+__device__ __forceinline__ bool allowed(const uint8_t* bitset, int64_t bits, int64_t id) {
+  if (!bitset) return true;
+  if (id < 0 || id >= bits) return false;
+  return (bitset[id >> 3] >> (id & 7)) & 1u;
+}
+
+// The exact score of one pair, sequential over the dimensions (used for the reported
+// distances; it repeats the scan's arithmetic operation for operation).
+__device__ float exact_score(int metric, const float* q, float qn, const float* y, float yn,
+                             int dim) {
+  float acc = 0.f;
+  int cnt = 0;
+  switch (acc_kind(metric)) {
+    case kAccDot:
+      for (int d = 0; d < dim; ++d) accumulate<kAccDot>(acc, cnt, q[d], y[d]);
+      return finish<kAccDot>(metric, acc, cnt, qn, yn);
+    case kAccHamming:
+      for (int d = 0; d < dim; ++d) accumulate<kAccHamming>(acc, cnt, q[d], y[d]);
+      return finish<kAccHamming>(metric, acc, cnt, qn, yn);
+    case kAccLp:
+      for (int d = 0; d < dim; ++d) accumulate<kAccLp>(acc, cnt, q[d], y[d]);
+      return finish<kAccLp>(metric, acc, cnt, qn, yn);
+    default:
+      for (int d = 0; d < dim; ++d) accumulate<kAccL2>(acc, cnt, q[d], y[d]);
+      return finish<kAccL2>(metric, acc, cnt, qn, yn);
+  }
+}
+
+// Inserts key x into the ascending list[0..K) held in shared memory (its last entry drops out).
+// Lane l owns entries [l*S, l*S + S), S = ceil(K / 32) <= 8. Keys are unique, so the insertion
+// point is the count of smaller entries.
+__device__ __forceinline__ void warp_insert(uint64_t* list, int K, uint64_t x, int lane) {
+  const int S = (K + 31) >> 5;
+  const int base = lane * S;
+  uint64_t vals[kIvfMaxSelect / 32];
+  int less = 0;
+#pragma unroll
+  for (int s = 0; s < kIvfMaxSelect / 32; ++s) {
+    if (s < S) {
+      const int i = base + s;
+      vals[s] = i < K ? list[i] : keys::kEmptyKey;
+      less += static_cast<int>(i < K && vals[s] < x);
+    }
+  }
+  const uint64_t prev = (base > 0 && base - 1 < K) ? list[base - 1] : keys::kEmptyKey;
+  const int pos = __reduce_add_sync(0xffffffffu, less);
+  __syncwarp();
+#pragma unroll
+  for (int s = 0; s < kIvfMaxSelect / 32; ++s) {
+    if (s < S) {
+      const int i = base + s;
+      if (i < K && i >= pos) list[i] = i == pos ? x : (s == 0 ? prev : vals[s - 1]);
+    }
+  }
+  __syncwarp();
+}
+
+// Work item -> list: the largest c with item_off[c] <= item.
+__device__ __forceinline__ int list_of_item(const int* item_off, int nlist, int item) {
+  int lo = 0, hi = nlist - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (item_off[mid] <= item)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  return lo;
+}
+
+// One work item = one list c and up to kIvfPairs (query, probe) pairs that probe it. The list's
+// rows are scored in tiles of kIvfRows against all the item's queries (4 x 4 per thread, every
+// score accumulated over d = 0, 1, ... with separately rounded operations).
+//   SORT = false: each pair keeps its k_sel smallest keys in shared memory, written to cand.
+//   SORT = true:  every candidate's key is written to its place in the query's segment.
+template <int ACC, bool SORT>
+__global__ void __launch_bounds__(kThreads)
+    ivf_scan_kernel(const __grid_constant__ IvfScanParams p) {
+  extern __shared__ __align__(16) uint8_t dyn[];
+  uint64_t* lists = reinterpret_cast<uint64_t*>(dyn);
+  __shared__ float As[kTK][kPadP];
+  __shared__ float Bs[kTK][kPadR];
+  __shared__ float S[SORT ? 1 : kIvfPairs][kPadR];
+  __shared__ int s_q[kIvfPairs];
+  __shared__ int s_pair[kIvfPairs];
+  __shared__ uint32_t s_cum[kIvfPairs];
+  __shared__ float s_qn[kIvfPairs];
+  __shared__ int64_t s_seg[SORT ? kIvfPairs : 1];
+
+  const int item = static_cast<int>(blockIdx.x);
+  if (item >= p.item_off[p.nlist]) return;
+  const int c = list_of_item(p.item_off, p.nlist, item);
+  const int chunk = item - p.item_off[c];
+  const int pair0 = p.list_q_off[c] + chunk * kIvfPairs;
+  const int npairs = min(kIvfPairs, p.list_q_off[c + 1] - pair0);
+  const int64_t row0 = p.list_off[c];
+  const int64_t L = p.list_off[c + 1] - row0;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int dim = p.dim;
+
+  if (tid < kIvfPairs) {
+    if (tid < npairs) {
+      const int pr = p.pair_of[pair0 + tid];
+      const int q = pr / p.nprobe, pp = pr - q * p.nprobe;
+      s_q[tid] = q;
+      s_pair[tid] = pr;
+      s_cum[tid] = p.cum[static_cast<int64_t>(q) * (p.nprobe + 1) + pp];
+      s_qn[tid] = p.q_norm[q];
+      if constexpr (SORT) s_seg[tid] = p.seg_base[q];
+    } else {
+      s_q[tid] = -1;
+      s_pair[tid] = -1;
+      s_cum[tid] = 0;
+      s_qn[tid] = 0.f;
+    }
+  }
+  if constexpr (!SORT) {
+    for (int e = tid; e < npairs * p.k_sel; e += kThreads) lists[e] = keys::kEmptyKey;
+  }
+  __syncthreads();
+
+  for (int64_t j0 = 0; j0 < L; j0 += kIvfRows) {
+    float acc[4][4];
+    int cnt[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        acc[a][b] = 0.f;
+        cnt[a][b] = 0;
+      }
+    for (int t0 = 0; t0 < dim; t0 += kTK) {
+      // loads run along the dimensions (16 consecutive floats per row)
+      for (int e = tid; e < kIvfPairs * kTK; e += kThreads) {
+        const int r = e / kTK, cc = e % kTK;
+        const int q = s_q[r];
+        As[cc][r] = (q >= 0 && t0 + cc < dim) ? p.queries[static_cast<int64_t>(q) * dim + t0 + cc]
+                                              : 0.f;
+      }
+      for (int e = tid; e < kIvfRows * kTK; e += kThreads) {
+        const int r = e / kTK, cc = e % kTK;
+        const int64_t j = j0 + r;
+        Bs[cc][r] = (j < L && t0 + cc < dim) ? p.rows[(row0 + j) * dim + t0 + cc] : 0.f;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int t = 0; t < kTK; ++t) {
+        float av[4], bv[4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) av[a] = As[t][ty + 16 * a];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) bv[b] = Bs[t][tx + 16 * b];
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+          for (int b = 0; b < 4; ++b) accumulate<ACC>(acc[a][b], cnt[a][b], av[a], bv[b]);
+      }
+      __syncthreads();
+    }
+    // scores (+inf for filtered rows, indexes.cpp:336-339)
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      const int pi = ty + 16 * a;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int rj = tx + 16 * b;
+        const int64_t j = j0 + rj;
+        if (pi < npairs && j < L) {
+          float v = finish<ACC>(p.metric, acc[a][b], cnt[a][b], s_qn[pi], p.row_norm[row0 + j]);
+          if (p.bitset && !allowed(p.bitset, p.bitset_bits, p.row_ids[row0 + j]))
+            v = __int_as_float(0x7f800000);
+          if constexpr (SORT) {
+            const uint32_t pos = s_cum[pi] + static_cast<uint32_t>(j);
+            p.keys[s_seg[pi] + pos] = keys::make_key(v, pos);
+          } else {
+            S[pi][rj] = v;
+          }
+        }
+      }
+    }
+    if constexpr (!SORT) {
+      __syncthreads();
+      // warp w keeps the lists of pairs 8w .. 8w+7
+      for (int i = 0; i < kIvfPairs / 8; ++i) {
+        const int pi = warp * (kIvfPairs / 8) + i;
+        if (pi >= npairs) break;
+        uint64_t* list = lists + static_cast<size_t>(pi) * p.k_sel;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int rj = lane + 32 * half;
+          const int64_t j = j0 + rj;
+          const uint64_t key = j < L ? keys::make_key(S[pi][rj], s_cum[pi] + static_cast<uint32_t>(j))
+                                     : keys::kEmptyKey;
+          uint32_t mask = __ballot_sync(0xffffffffu, key < list[p.k_sel - 1]);
+          while (mask) {
+            const int src = __ffs(mask) - 1;
+            mask &= mask - 1;
+            const uint64_t x = __shfl_sync(0xffffffffu, key, src);
+            if (x < list[p.k_sel - 1]) warp_insert(list, p.k_sel, x, lane);
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  if constexpr (!SORT) {
+    for (int e = tid; e < npairs * p.k_sel; e += kThreads) {
+      const int pi = e / p.k_sel, i = e - pi * p.k_sel;
+      p.cand[static_cast<size_t>(s_pair[pi]) * p.k_sel + i] = lists[e];
+    }
+  }
+}
+
+__global__ void probe_offsets_kernel(const int64_t* __restrict__ probe, int64_t nq, int nprobe,
+                                     const int64_t* __restrict__ list_off, int nlist,
+                                     uint32_t* __restrict__ cum, int* __restrict__ list_q_count) {
+  const int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (q >= nq) return;
+  uint32_t acc = 0;
+  uint32_t* out = cum + q * (nprobe + 1);
+  for (int pp = 0; pp < nprobe; ++pp) {
+    const int64_t c = probe[q * nprobe + pp];
+    out[pp] = acc;
+    if (c >= 0 && c < nlist) {
+      acc += static_cast<uint32_t>(list_off[c + 1] - list_off[c]);
+      atomicAdd(&list_q_count[c], 1);
+    }
+  }
+  out[nprobe] = acc;
+}
+
+__global__ void group_pairs_kernel(const int64_t* __restrict__ probe, int64_t nq, int nprobe,
+                                   int nlist, const int* __restrict__ list_q_off,
+                                   int* __restrict__ cursor, int* __restrict__ pair_of) {
+  const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (e >= nq * nprobe) return;
+  const int64_t c = probe[e];
+  if (c < 0 || c >= nlist) return;
+  const int slot = atomicAdd(&cursor[c], 1);
+  pair_of[list_q_off[c] + slot] = static_cast<int>(e);
+}
+
+__global__ void item_counts_kernel(const int* __restrict__ list_q_count, int nlist,
+                                   int* __restrict__ item_count) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c > nlist) return;
+  item_count[c] = c < nlist ? (list_q_count[c] + kIvfPairs - 1) / kIvfPairs : 0;
+}
+
+// One warp per query: the k smallest keys of its candidates (merged from the per-pair lists in
+// select mode, the head of its sorted segment in sort mode), then ids and exact distances.
+__global__ void ivf_emit_kernel(const __grid_constant__ IvfScanParams p,
+                                const uint64_t* __restrict__ sorted_keys, int64_t k,
+                                int64_t* __restrict__ neighbors, float* __restrict__ distances) {
+  extern __shared__ __align__(16) uint8_t dyn[];
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const int64_t q = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + wib;
+  if (q >= p.nq) return;
+  const int np = p.nprobe;
+  const uint32_t* cum = p.cum + q * (np + 1);
+  const uint32_t total = cum[np];
+  const uint64_t* best;
+  if (sorted_keys == nullptr) {
+    uint64_t* list = reinterpret_cast<uint64_t*>(dyn) + static_cast<size_t>(wib) * k;
+    for (int64_t i = lane; i < k; i += 32) list[i] = keys::kEmptyKey;
+    __syncwarp();
+    const int K = static_cast<int>(k);
+    const int64_t n_in = static_cast<int64_t>(np) * p.k_sel;
+    const uint64_t* in = p.cand + q * n_in;
+    for (int64_t b = 0; b < n_in; b += 32) {
+      const uint64_t key = b + lane < n_in ? in[b + lane] : keys::kEmptyKey;
+      uint32_t mask = __ballot_sync(0xffffffffu, key < list[K - 1]);
+      while (mask) {
+        const int src = __ffs(mask) - 1;
+        mask &= mask - 1;
+        const uint64_t x = __shfl_sync(0xffffffffu, key, src);
+        if (x < list[K - 1]) warp_insert(list, K, x, lane);
+      }
+    }
+    best = list;
+  } else {
+    best = sorted_keys + p.seg_base[q];
+  }
+  const int64_t kk = static_cast<int64_t>(total) < k ? static_cast<int64_t>(total) : k;
+  const float inf = __int_as_float(0x7f800000);
+  for (int64_t t = lane; t < k; t += 32) {
+    int64_t id = -1;
+    float d = inf;
+    const uint64_t key = t < kk ? best[t] : keys::kEmptyKey;
+    if (t < kk && key != keys::kEmptyKey) {
+      const uint32_t pos = keys::key_id(key);
+      // probe of this position: the last pp with cum[pp] <= pos
+      int lo = 0, hi = np - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (cum[mid] <= pos)
+          lo = mid;
+        else
+          hi = mid - 1;
+      }
+      const int64_t c = p.probe[q * np + lo];
+      const int64_t g = p.list_off[c] + (pos - cum[lo]);
+      id = p.row_ids[g];
+      const float* qr = p.queries + q * p.dim;
+      float v = exact_score(p.metric, qr, p.q_norm[q], p.rows + g * p.dim, p.row_norm[g], p.dim);
+      if (p.bitset && !allowed(p.bitset, p.bitset_bits, id)) v = inf;
+      d = p.metric == kRawIp ? -v : v;
+    }
+    neighbors[q * k + t] = id;
+    distances[q * k + t] = d;
+  }
+}
+
+__global__ void gather_list_rows_kernel(const float* __restrict__ x, int64_t n_x, int dim,
+                                        const int64_t* __restrict__ ids, int64_t n_rows,
+                                        float* __restrict__ rows, float* __restrict__ row_norm) {
+  const int lane = threadIdx.x & 31;
+  const int64_t g = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (g >= n_rows) return;
+  const int64_t id = ids[g];
+  const bool ok = id >= 0 && id < n_x;
+  float* dst = rows + g * dim;
+  for (int d = lane; d < dim; d += 32) dst[d] = ok ? x[id * dim + d] : 0.f;
+  __syncwarp();
+  if (lane == 0) {
+    float s = 0.f;  // nrm2sq (internal.hpp:221-225): sequential
+    for (int d = 0; d < dim; ++d) s = __fadd_rn(s, __fmul_rn(dst[d], dst[d]));
+    row_norm[g] = s;
+  }
+}
+
+// One warp per score row: the K smallest (score, column) keys by warp insertion into a list in
+// shared memory, then their columns.
+__global__ void coarse_select_kernel(const float* __restrict__ scores, int64_t rows, int cols,
+                                     int K, int64_t* __restrict__ probe) {
+  extern __shared__ __align__(16) uint8_t dyn[];
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + wib;
+  if (r >= rows) return;
+  uint64_t* list = reinterpret_cast<uint64_t*>(dyn) + static_cast<size_t>(wib) * K;
+  for (int i = lane; i < K; i += 32) list[i] = keys::kEmptyKey;
+  __syncwarp();
+  const float* row = scores + r * cols;
+  for (int b = 0; b < cols; b += 32) {
+    const int j = b + lane;
+    const uint64_t key = j < cols ? keys::make_key(row[j], static_cast<uint32_t>(j)) : keys::kEmptyKey;
+    uint32_t mask = __ballot_sync(0xffffffffu, key < list[K - 1]);
+    while (mask) {
+      const int src = __ffs(mask) - 1;
+      mask &= mask - 1;
+      const uint64_t x = __shfl_sync(0xffffffffu, key, src);
+      if (x < list[K - 1]) warp_insert(list, K, x, lane);
+    }
+  }
+  for (int i = lane; i < K; i += 32) {
+    const uint64_t key = list[i];
+    probe[r * K + i] = key == keys::kEmptyKey ? -1 : static_cast<int64_t>(keys::key_id(key));
+  }
+}
+
+__global__ void totals_kernel(const uint32_t* __restrict__ cum, int64_t nq, int nprobe,
+                              int64_t* __restrict__ totals) {
+  const int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (q > nq) return;
+  totals[q] = q < nq ? static_cast<int64_t>(cum[q * (nprobe + 1) + nprobe]) : 0;
+}
+
+__global__ void seg_bounds_kernel(const int64_t* __restrict__ seg_base,
+                                  const uint32_t* __restrict__ cum, int64_t nq, int nprobe,
+                                  int* __restrict__ seg_begin, int* __restrict__ seg_end) {
+  const int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (q >= nq) return;
+  seg_begin[q] = static_cast<int>(seg_base[q]);
+  seg_end[q] = static_cast<int>(seg_base[q] + cum[q * (nprobe + 1) + nprobe]);
+}
+
+template <bool SORT>
+cudaError_t launch_scan(const IvfScanParams& p, int64_t grid, cudaStream_t stream) {
+  if (grid <= 0) return cudaSuccess;
+  if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
+  const size_t dyn = SORT ? 0 : static_cast<size_t>(kIvfPairs) * p.k_sel * sizeof(uint64_t);
+  const dim3 g(static_cast<unsigned>(grid));
+  auto run = [&](auto kern) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(dyn));
+    if (e != cudaSuccess) return e;
+    kern<<<g, kThreads, dyn, stream>>>(p);
+    return cudaGetLastError();
+  };
+  switch (acc_kind(p.metric)) {
+    case kAccDot:
+      return run(ivf_scan_kernel<kAccDot, SORT>);
+    case kAccHamming:
+      return run(ivf_scan_kernel<kAccHamming, SORT>);
+    case kAccLp:
+      return run(ivf_scan_kernel<kAccLp, SORT>);
+    default:
+      return run(ivf_scan_kernel<kAccL2, SORT>);
+  }
+}
+
+}  // namespace
+
+int64_t ivf_max_items(int64_t nq, int nprobe, int nlist) {
+  return nq * nprobe / kIvfPairs + nlist;
+}
+
+size_t ivf_select_smem(int k_sel) {
+  return static_cast<size_t>(kIvfPairs) * k_sel * sizeof(uint64_t);
+}
+
+cudaError_t launch_ivf_probe_offsets(const int64_t* probe, int64_t nq, int nprobe,
+                                     const int64_t* list_off, int nlist, uint32_t* cum,
+                                     int* list_q_count, cudaStream_t stream) {
+  probe_offsets_kernel<<<static_cast<unsigned>((nq + 127) / 128), 128, 0, stream>>>(
+      probe, nq, nprobe, list_off, nlist, cum, list_q_count);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ivf_group_pairs(const int64_t* probe, int64_t nq, int nprobe, int nlist,
+                                   const int* list_q_off, int* cursor, int* pair_of,
+                                   cudaStream_t stream) {
+  const int64_t n = nq * nprobe;
+  if (n <= 0) return cudaSuccess;
+  group_pairs_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(
+      probe, nq, nprobe, nlist, list_q_off, cursor, pair_of);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ivf_item_counts(const int* list_q_count, int nlist, int* item_count,
+                                   cudaStream_t stream) {
+  item_counts_kernel<<<static_cast<unsigned>((nlist + 1 + 255) / 256), 256, 0, stream>>>(
+      list_q_count, nlist, item_count);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ivf_scan_select(const IvfScanParams& p, int64_t grid, cudaStream_t stream) {
+  if (p.k_sel < 1 || p.k_sel > kIvfMaxSelect) return cudaErrorInvalidValue;
+  return launch_scan<false>(p, grid, stream);
+}
+
+cudaError_t launch_ivf_scan_sort(const IvfScanParams& p, int64_t grid, cudaStream_t stream) {
+  return launch_scan<true>(p, grid, stream);
+}
+
+constexpr int kEmitWarps = 8;
+
+size_t ivf_emit_smem(int64_t k) { return static_cast<size_t>(kEmitWarps) * k * sizeof(uint64_t); }
+
+cudaError_t launch_ivf_emit(const IvfScanParams& p, const uint64_t* sorted_keys, int64_t k,
+                            int64_t* neighbors, float* distances, cudaStream_t stream) {
+  constexpr int kWarps = kEmitWarps;
+  const size_t dyn = sorted_keys ? 0 : ivf_emit_smem(k);
+  cudaError_t e = cudaFuncSetAttribute(ivf_emit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(dyn));
+  if (e != cudaSuccess) return e;
+  ivf_emit_kernel<<<static_cast<unsigned>((p.nq + kWarps - 1) / kWarps), kWarps * 32, dyn,
+                    stream>>>(p, sorted_keys, k, neighbors, distances);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ivf_coarse_select(const float* scores, int64_t rows, int cols, int K,
+                                     int64_t* probe, cudaStream_t stream) {
+  if (K < 1 || K > kIvfMaxSelect) return cudaErrorInvalidValue;
+  if (rows <= 0) return cudaSuccess;
+  constexpr int kWarps = 8;
+  const size_t dyn = static_cast<size_t>(kWarps) * K * sizeof(uint64_t);
+  cudaError_t e = cudaFuncSetAttribute(coarse_select_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(dyn));
+  if (e != cudaSuccess) return e;
+  coarse_select_kernel<<<static_cast<unsigned>((rows + kWarps - 1) / kWarps), kWarps * 32, dyn,
+                         stream>>>(scores, rows, cols, K, probe);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ivf_totals(const uint32_t* cum, int64_t nq, int nprobe, int64_t* totals,
+                              cudaStream_t stream) {
+  totals_kernel<<<static_cast<unsigned>((nq + 1 + 255) / 256), 256, 0, stream>>>(cum, nq, nprobe,
+                                                                                totals);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ivf_seg_bounds(const int64_t* seg_base, const uint32_t* cum, int64_t nq,
+                                  int nprobe, int* seg_begin, int* seg_end, cudaStream_t stream) {
+  if (nq <= 0) return cudaSuccess;
+  seg_bounds_kernel<<<static_cast<unsigned>((nq + 255) / 256), 256, 0, stream>>>(
+      seg_base, cum, nq, nprobe, seg_begin, seg_end);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ivf_gather_rows(const float* x, int64_t n_x, int dim, const int64_t* ids,
+                                   int64_t n_rows, float* rows, float* row_norm,
+                                   cudaStream_t stream) {
+  if (n_rows <= 0) return cudaSuccess;
+  gather_list_rows_kernel<<<static_cast<unsigned>((n_rows + 7) / 8), 256, 0, stream>>>(
+      x, n_x, dim, ids, n_rows, rows, row_norm);
+  return cudaGetLastError();
+}
+
+}  // namespace prim
+}  // namespace ovvs

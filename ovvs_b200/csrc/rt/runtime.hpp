@@ -15,6 +15,7 @@
 #include <cstdint>
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "nccl_dl.hpp"
 #include "ovvs/ovvs.h"
@@ -49,6 +50,12 @@ class DeviceBuffer {
   // Ensures at least `bytes` are allocated (contents are not preserved on growth).
   cudaError_t reserve(size_t bytes);
   void release();
+  // Exchanges the allocations of two buffers (used to grow a buffer while keeping its data).
+  void swap(DeviceBuffer& o) noexcept {
+    std::swap(ptr_, o.ptr_);
+    std::swap(bytes_, o.bytes_);
+    std::swap(device_, o.device_);
+  }
   void* get() const { return ptr_; }
   size_t size() const { return bytes_; }
   template <class T>
@@ -83,6 +90,23 @@ enum WorkSlot : int {
   kWsShardGid,
   kWsGatherRank,
   kWsGatherGid,
+  kWsIvfQueryNorm,  // IVF-Flat search: query norms
+  kWsIvfScores,     // coarse scores [queries x nlist]
+  kWsIvfProbe,      // probed lists [queries x nprobe]
+  kWsIvfProbeVal,
+  kWsIvfCum,        // per-query positions of the probed lists
+  kWsIvfListCount,  // pairs per list, their offsets, fill cursors
+  kWsIvfListOff,
+  kWsIvfCursor,
+  kWsIvfPairs,
+  kWsIvfItemCount,
+  kWsIvfItemOff,
+  kWsIvfCand,       // per-pair candidate lists (select mode) / candidate keys (sort mode)
+  kWsIvfCand2,
+  kWsIvfSeg,        // sort mode: segment bases and bounds
+  kWsIvfSegBegin,
+  kWsIvfSegEnd,
+  kWsIvfTmp,        // CUB temporary storage
   kWsCount
 };
 

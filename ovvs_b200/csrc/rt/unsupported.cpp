@@ -1,40 +1,10 @@
-// Entry points of the ovvs ABI outside this library's scope (IVF, graph indexes, quantizers,
+// Entry points of the ovvs ABI outside this library's scope (IVF-PQ / RaBitQ, graph indexes, quantizers,
 // PCA, SLINK/spectral). They exist so that binaries and bindings built
 // against the reference ABI still link and load; each returns OVVS_STATUS_UNSUPPORTED (Destroy
 // functions accept any handle, as none can have been created, and return OVVS_STATUS_SUCCESS).
 #include "ovvs/ovvs.h"
 
 extern "C" {
-
-ovvsStatus ovvsIvfFlatBuild(ovvsResources_t res, const float* dataset, int64_t n, int64_t dim, ovvsMetric metric, int32_t nlist, ovvsIvfFlatIndex_t* index) {
-  (void)res; (void)dataset; (void)n; (void)dim; (void)metric; (void)nlist; (void)index;
-  return OVVS_STATUS_UNSUPPORTED;
-}
-
-ovvsStatus ovvsIvfFlatSearch(ovvsResources_t res, ovvsIvfFlatIndex_t index, const float* queries, int64_t nq, int64_t k, int32_t nprobe, const uint8_t* bitset, int64_t* neighbors, float* distances) {
-  (void)res; (void)index; (void)queries; (void)nq; (void)k; (void)nprobe; (void)bitset; (void)neighbors; (void)distances;
-  return OVVS_STATUS_UNSUPPORTED;
-}
-
-ovvsStatus ovvsIvfFlatSerialize(ovvsIvfFlatIndex_t index, const char* path) {
-  (void)index; (void)path;
-  return OVVS_STATUS_UNSUPPORTED;
-}
-
-ovvsStatus ovvsIvfFlatDeserialize(ovvsResources_t res, const char* path, ovvsIvfFlatIndex_t* index) {
-  (void)res; (void)path; (void)index;
-  return OVVS_STATUS_UNSUPPORTED;
-}
-
-ovvsStatus ovvsIvfFlatExtend(ovvsResources_t res, ovvsIvfFlatIndex_t index, const float* extra, int64_t nextra) {
-  (void)res; (void)index; (void)extra; (void)nextra;
-  return OVVS_STATUS_UNSUPPORTED;
-}
-
-ovvsStatus ovvsIvfFlatDestroy(ovvsIvfFlatIndex_t index) {
-  (void)index;
-  return OVVS_STATUS_SUCCESS;
-}
 
 ovvsStatus ovvsIvfPqBuild(ovvsResources_t res, const float* dataset, int64_t n, int64_t dim, ovvsMetric metric, int32_t nlist, int32_t pq_m, int32_t pq_nbits, ovvsIvfPqIndex_t* index) {
   (void)res; (void)dataset; (void)n; (void)dim; (void)metric; (void)nlist; (void)pq_m; (void)pq_nbits; (void)index;

@@ -22,6 +22,8 @@ def _load_npz_cases(name):
     z = np.load(os.path.join(GOLDEN, name), allow_pickle=False)
     cases = {}
     for key in z.files:
+        if "__" not in key:
+            continue
         case, field = key.split("__", 1)
         cases.setdefault(case, {})[field] = z[key]
     return cases
@@ -73,3 +75,8 @@ def gpu(ovvs):
 @pytest.fixture(scope="session")
 def golden_prims():
     return _load_npz_cases("prims.npz")
+
+
+@pytest.fixture(scope="session")
+def golden_ivf():
+    return _load_npz_cases("ivf_flat.npz")

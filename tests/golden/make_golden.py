@@ -201,6 +201,86 @@ def write_prims(ref, rng):
     np.savez_compressed(os.path.join(OUT, "prims.npz"), **out)
 
 
+def ivf_cases(rng):
+    """(name, x, extra, nlist, metric, queries, k, nprobe, bitset) for ovvsIvfFlat*."""
+    cases = []
+    # the reference's own IVF-Flat scenarios (tests/test_neighbors.cpp)
+    cases.append(("recall_l2", make_data(80, 8, 200), None, 8, "l2", make_data(6, 8, 201), 5, 8,
+                  None))
+    tri = np.array([[1, 0], [0, 1], [-1, 0], [0.5, 0.5]], np.float32)
+    cases.append(("known_ip", tri, None, 1, "inner_product", np.array([[1, 0]], np.float32), 2, 1,
+                  None))
+    allx = make_data(45, 8, 450)
+    cases.append(("serialize_extend", allx[:40], allx[40:], 8, "l2", make_data(4, 8, 451), 4, 8,
+                  None))
+    # every metric (unknown values score as squared L2), few probes
+    x = rng.standard_normal((400, 12)).astype(np.float32)
+    q = rng.standard_normal((20, 12)).astype(np.float32)
+    for metric in ("l2", "l2_sqrt", "inner_product", "cosine", "hamming", "lp", "unknown7"):
+        cases.append((f"metric_{metric}", x, None, 10, metric, q, 7, 3, None))
+    # filtered rows score +inf and can still be returned
+    x = rng.standard_normal((300, 16)).astype(np.float32)
+    q = rng.standard_normal((15, 16)).astype(np.float32)
+    bits = np.zeros((300 + 7) // 8, np.uint8)
+    for i in range(0, 300, 3):
+        bits[i >> 3] |= 1 << (i & 7)
+    cases.append(("bitset_l2", x, None, 6, "l2", q, 9, 2, bits))
+    few = np.zeros((300 + 7) // 8, np.uint8)
+    for i in (4, 150, 299):
+        few[i >> 3] |= 1 << (i & 7)
+    cases.append(("bitset_ip_few", x, None, 6, "inner_product", q, 9, 6, few))
+    # more neighbours than candidates: -1 / +inf padding
+    x = rng.random((60, 4), dtype=np.float32)
+    cases.append(("k_exceeds_candidates", x, None, 6, "l2", rng.random((5, 4), dtype=np.float32),
+                  40, 1, None))
+    # nprobe clamped to [1, nlist]
+    cases.append(("nprobe_clamped", x, None, 5, "l2", rng.random((5, 4), dtype=np.float32), 6,
+                  100, None))
+    cases.append(("nprobe_zero", x, None, 5, "cosine", rng.random((5, 4), dtype=np.float32), 6, 0,
+                  None))
+    # nlist above n
+    cases.append(("nlist_gt_n", rng.random((5, 3), dtype=np.float32), None, 16, "l2",
+                  rng.random((4, 3), dtype=np.float32), 3, 2, None))
+    # duplicate rows: equal scores, ties to the earlier position in the probe concatenation
+    base = np.round(rng.standard_normal((40, 6)), 1).astype(np.float32)
+    dup = np.concatenate([base, base[:20], base[5:15]])
+    cases.append(("duplicates_ip", dup, None, 4, "inner_product",
+                  np.round(rng.standard_normal((8, 6)), 1).astype(np.float32), 12, 4, None))
+    cases.append(("duplicates_l2", dup, None, 4, "l2",
+                  np.round(rng.standard_normal((8, 6)), 1).astype(np.float32), 12, 2, None))
+    # k above the shared-memory list limit (the sort path)
+    x = rng.standard_normal((700, 8)).astype(np.float32)
+    cases.append(("large_k", x, None, 4, "l2", rng.standard_normal((6, 8)).astype(np.float32),
+                  300, 3, None))
+    return cases
+
+
+def write_ivf(ref, rng):
+    out = {}
+    names = []
+    for (name, x, extra, nlist, metric, q, k, nprobe, bits) in ivf_cases(rng):
+        m = METRIC_IDS[metric]
+        nb, ds, parts = ref.ivf_flat(x, nlist, m, q, k, nprobe, bitset=bits, extra=extra)
+        p = f"{name}__"
+        names.append(name)
+        out[p + "x"] = np.ascontiguousarray(x, np.float32)
+        out[p + "extra"] = (np.zeros((0, x.shape[1]), np.float32) if extra is None
+                            else np.ascontiguousarray(extra, np.float32))
+        out[p + "nlist"] = np.array(nlist)
+        out[p + "metric"] = np.array(m)
+        out[p + "queries"] = np.ascontiguousarray(q, np.float32)
+        out[p + "k"] = np.array(k)
+        out[p + "nprobe"] = np.array(nprobe)
+        out[p + "bitset"] = np.zeros(0, np.uint8) if bits is None else bits
+        out[p + "neighbors"] = nb
+        out[p + "distances"] = ds
+        out[p + "centroids"] = parts["centroids"]
+        out[p + "sizes"] = parts["sizes"]
+        out[p + "ids"] = parts["ids"]
+    out["cases"] = np.array(names)
+    np.savez_compressed(os.path.join(OUT, "ivf_flat.npz"), **out)
+
+
 def main():
     ref = Reference()
     rng = np.random.default_rng(20261201)
@@ -242,8 +322,12 @@ def main():
                         bitset_n=np.array(20), bitset=bs,
                         version=np.array(ref.lib.ovvsGetVersion().decode()))
     write_prims(ref, np.random.default_rng(20261202))
+    write_ivf(ref, np.random.default_rng(20261203))
     print("wrote", sorted(f for f in os.listdir(OUT) if f.endswith(".npz")))
 
 
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] == ["ivf"]:  # only the IVF-Flat fixtures
+        write_ivf(Reference(), np.random.default_rng(20261203))
+    else:
+        main()

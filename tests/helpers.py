@@ -48,3 +48,16 @@ def assert_search_close(nb, ds, nb_ref, ds_ref, k_eff, exact_dist, rtol, what=""
         floor = atol_floor if atol_floor is not None else 0.0
         assert abs(float(ds[q, j]) - ref) <= rtol * max(abs(ref), floor) + 1e-30, (
             f"{what}: q={q} rank={j} {ds[q, j]} vs {ref} beyond near-tie tolerance")
+
+
+def ivf_extend_lists(centroids, sizes, ids, n_old, labels, nlist):
+    """The lists after ovvsIvfFlatExtend (indexes.cpp:447-455): each new row (id n_old + i) is
+    appended to the list of its label, in row order. Returns (sizes, ids)."""
+    off = np.concatenate([[0], np.cumsum(sizes)])
+    new_sizes, new_ids = [], []
+    for c in range(nlist):
+        add = n_old + np.nonzero(labels == c)[0]
+        new_ids.append(np.concatenate([ids[off[c]:off[c + 1]], add]).astype(np.int64))
+        new_sizes.append(int(off[c + 1] - off[c]) + add.size)
+    return np.array(new_sizes, np.int64), (np.concatenate(new_ids) if new_ids
+                                            else np.zeros(0, np.int64))

@@ -166,8 +166,11 @@ def test_out_of_scope_entry_points_are_unsupported(ovvs):
     h = ctypes.c_void_p()
     x = np.zeros((8, 4), np.float32)
     xp = ctypes.c_void_p(x.ctypes.data)
-    L.ovvsIvfFlatBuild.restype = ctypes.c_int
-    assert L.ovvsIvfFlatBuild(res._h, xp, ctypes.c_int64(8), ctypes.c_int64(4), 0, 2, ctypes.byref(h)) == 3
+    L.ovvsIvfPqBuild.restype = ctypes.c_int
+    assert L.ovvsIvfPqBuild(res._h, xp, ctypes.c_int64(8), ctypes.c_int64(4), 0, 2, 2, 8,
+                            ctypes.byref(h)) == 3
+    # IVF-Flat is on the B200 path: without a GPU it reports the device as unavailable
+    assert L.ovvsIvfFlatBuild(res._h, xp, 8, 4, 0, 2, ctypes.byref(h)) == 7
     assert L.ovvsCagraBuild(res._h, xp, ctypes.c_int64(8), ctypes.c_int64(4), 0, 4, 8, ctypes.byref(h)) == 3
     assert L.ovvsIvfFlatDestroy(None) == 0
     assert L.ovvsSyclEnabled() == 0

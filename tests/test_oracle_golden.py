@@ -9,7 +9,7 @@ import os
 import numpy as np
 import pytest
 
-from tests.helpers import assert_search_equal, same_bits
+from tests.helpers import assert_search_equal, ivf_extend_lists, same_bits
 
 
 def _brute_case(c, oracle):
@@ -108,3 +108,21 @@ def test_primitive_cases_bit_exact(golden_prims, oracle):
         else:
             raise AssertionError(name)
     assert kinds == {"gemm", "topk", "gather", "pw", "an"}
+
+
+def test_ivf_flat_cases_bit_exact(golden_ivf, oracle):
+    """IVF-Flat build (k-means lists) and search (indexes.cpp:281-358), extension included."""
+    assert len(golden_ivf) >= 18
+    for name, c in golden_ivf.items():
+        x, extra = c["x"], c["extra"]
+        cents, sizes, ids = oracle.ivf_flat_build(x, int(c["nlist"]))
+        if extra.shape[0]:
+            labels, _ = oracle.kmeans_predict(cents, extra)
+            sizes, ids = ivf_extend_lists(cents, sizes, ids, x.shape[0], labels, cents.shape[0])
+            x = np.concatenate([x, extra])
+        assert np.all(same_bits(cents, c["centroids"])), name
+        assert np.array_equal(sizes, c["sizes"]) and np.array_equal(ids, c["ids"]), name
+        bits = c["bitset"] if c["bitset"].size else None
+        nb, ds = oracle.ivf_flat_search(x, int(c["metric"]), cents, sizes, ids, c["queries"],
+                                        int(c["k"]), int(c["nprobe"]), bits)
+        assert_search_equal(nb, ds, c["neighbors"], c["distances"], what=name)
