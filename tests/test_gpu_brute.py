@@ -150,6 +150,26 @@ def test_mixture_fp16_l2(ovvs, gpu, oracle):
                 kind="mixture", fp16_queries=True)
 
 
+@pytest.mark.parametrize("metric,dtype,k", [("l2", "f32", 1), ("inner_product", "f16", 32),
+                                            ("cosine", "f32", 10), ("l2_sqrt", "f16", 7),
+                                            ("hamming", "f32", 5)])
+def test_small_batch_sampled_bound(metric, dtype, k, ovvs, gpu, oracle):
+    """Small batches over a larger database: the work items of one query pair-tile all run at once
+    (one wave), so every item fills its lists from nothing."""
+    _run_parity(ovvs, gpu, oracle, metric, dtype, n=200_000, dim=48, nq=100, k=k, seed=77,
+                kind="mixture")
+
+
+def test_small_batch_sampled_bound_bitset(ovvs, gpu, oracle):
+    """Small batch with few allowed rows (fewer than k in many work items: their lists hold
+    filtered rows at +inf) and with more."""
+    rng = np.random.default_rng(8)
+    n = 200_000
+    for frac in (0.001, 0.05):
+        bs = ovvs.bitset_from_allow_list(n, np.nonzero(rng.random(n) < frac)[0])
+        _run_parity(ovvs, gpu, oracle, "l2", "f32", n=n, dim=40, nq=60, k=32, seed=9, bitset=bs)
+
+
 def test_bitset_filtering(ovvs, gpu, oracle):
     rng = np.random.default_rng(5)
     n = 9000
