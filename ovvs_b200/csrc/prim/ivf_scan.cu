@@ -10,8 +10,9 @@ namespace prim {
 namespace {
 
 constexpr int kThreads = 256;  // 16 x 16 threads, 4 x 4 (pair, row) scores each (strided by 16)
-constexpr int kTK = 16;        // K slab staged in shared memory
-constexpr int kPadP = kIvfPairs + 1;
+constexpr int kTK = 32;        // K slab staged in shared memory (row-major, 8 float4 per row)
+constexpr int kSlabStride = kTK + 4;  // floats per staged row: 16-byte aligned, float4 reads of
+                                      // 16 consecutive rows fall on distinct bank groups
 constexpr int kPadR = kIvfRows + 1;
 
 // ovvsMetric values (ovvs.h)
@@ -136,6 +137,23 @@ __device__ __forceinline__ void warp_insert(uint64_t* list, int K, uint64_t x, i
   __syncwarp();
 }
 
+// warp_insert for K <= 32: one entry per lane.
+__device__ __forceinline__ void warp_insert_small(uint64_t* list, int K, uint64_t x, int lane) {
+  const uint64_t v = lane < K ? list[lane] : keys::kEmptyKey;
+  const int pos = __popc(__ballot_sync(0xffffffffu, v < x));
+  const uint64_t up = __shfl_up_sync(0xffffffffu, v, 1);
+  __syncwarp();
+  if (lane < K && lane >= pos) list[lane] = lane == pos ? x : up;
+  __syncwarp();
+}
+
+__device__ __forceinline__ void insert_key(uint64_t* list, int K, uint64_t x, int lane) {
+  if (K <= 32)
+    warp_insert_small(list, K, x, lane);
+  else
+    warp_insert(list, K, x, lane);
+}
+
 // Work item -> list: the largest c with item_off[c] <= item.
 __device__ __forceinline__ int list_of_item(const int* item_off, int nlist, int item) {
   int lo = 0, hi = nlist - 1;
@@ -151,16 +169,73 @@ __device__ __forceinline__ int list_of_item(const int* item_off, int nlist, int 
 
 // One work item = one list c and up to kIvfPairs (query, probe) pairs that probe it. The list's
 // rows are scored in tiles of kIvfRows against all the item's queries (4 x 4 per thread, every
-// score accumulated over d = 0, 1, ... with separately rounded operations).
+// score accumulated over d = 0, 1, ... with separately rounded operations; zero padding past dim
+// adds +0 products, which leave every metric's sum unchanged).
 //   SORT = false: each pair keeps its k_sel smallest keys in shared memory, written to cand.
 //   SORT = true:  every candidate's key is written to its place in the query's segment.
-template <int ACC, bool SORT>
+// Staging of one K slab: the item's query rows (by index) and the tile's list rows, row-major
+// with kSlabStride floats per row, zero outside the matrices. VEC: 16-byte loads (dim a multiple
+// of 4 and both bases 16-byte aligned); the slab is fetched into registers first (`fetch`) so its
+// global latency overlaps the previous slab's arithmetic, then stored (`store`).
+template <bool VEC>
+struct Stager {
+  static constexpr int kPer = VEC ? 2 : 8;  // float4 / float elements per thread per matrix
+  float4 ra[VEC ? 2 : 1], rb[VEC ? 2 : 1];
+  float sa[VEC ? 1 : 8], sb[VEC ? 1 : 8];
+  __device__ __forceinline__ void fetch(const IvfScanParams& p, const int* s_q, int64_t row0,
+                                        int64_t j0, int64_t L, int t0, int tid) {
+    const int dim = p.dim;
+    if constexpr (VEC) {
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int e = tid + kThreads * i, r = e >> 3, c = (e & 7) * 4;
+        const int q = s_q[r];
+        const bool in = t0 + c < dim;
+        ra[i] = (q >= 0 && in)
+                    ? *reinterpret_cast<const float4*>(p.queries + static_cast<int64_t>(q) * dim + t0 + c)
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+        const int64_t j = j0 + r;
+        rb[i] = (j < L && in) ? *reinterpret_cast<const float4*>(p.rows + (row0 + j) * dim + t0 + c)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int e = tid + kThreads * i, r = e >> 5, c = e & 31;
+        const int q = s_q[r];
+        const bool in = t0 + c < dim;
+        sa[i] = (q >= 0 && in) ? p.queries[static_cast<int64_t>(q) * dim + t0 + c] : 0.f;
+        const int64_t j = j0 + r;
+        sb[i] = (j < L && in) ? p.rows[(row0 + j) * dim + t0 + c] : 0.f;
+      }
+    }
+  }
+  __device__ __forceinline__ void store(float* As, float* Bs, int tid) {
+    if constexpr (VEC) {
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int e = tid + kThreads * i, r = e >> 3, c = (e & 7) * 4;
+        *reinterpret_cast<float4*>(As + r * kSlabStride + c) = ra[i];
+        *reinterpret_cast<float4*>(Bs + r * kSlabStride + c) = rb[i];
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int e = tid + kThreads * i, r = e >> 5, c = e & 31;
+        As[r * kSlabStride + c] = sa[i];
+        Bs[r * kSlabStride + c] = sb[i];
+      }
+    }
+  }
+};
+
+template <int ACC, bool SORT, bool VEC>
 __global__ void __launch_bounds__(kThreads)
     ivf_scan_kernel(const __grid_constant__ IvfScanParams p) {
   extern __shared__ __align__(16) uint8_t dyn[];
   uint64_t* lists = reinterpret_cast<uint64_t*>(dyn);
-  __shared__ float As[kTK][kPadP];
-  __shared__ float Bs[kTK][kPadR];
+  __shared__ __align__(16) float As[kIvfPairs * kSlabStride];
+  __shared__ __align__(16) float Bs[kIvfRows * kSlabStride];
   __shared__ float S[SORT ? 1 : kIvfPairs][kPadR];
   __shared__ int s_q[kIvfPairs];
   __shared__ int s_pair[kIvfPairs];
@@ -211,33 +286,33 @@ __global__ void __launch_bounds__(kThreads)
         acc[a][b] = 0.f;
         cnt[a][b] = 0;
       }
+    Stager<VEC> st;
+    st.fetch(p, s_q, row0, j0, L, 0, tid);
     for (int t0 = 0; t0 < dim; t0 += kTK) {
-      // loads run along the dimensions (16 consecutive floats per row)
-      for (int e = tid; e < kIvfPairs * kTK; e += kThreads) {
-        const int r = e / kTK, cc = e % kTK;
-        const int q = s_q[r];
-        As[cc][r] = (q >= 0 && t0 + cc < dim) ? p.queries[static_cast<int64_t>(q) * dim + t0 + cc]
-                                              : 0.f;
-      }
-      for (int e = tid; e < kIvfRows * kTK; e += kThreads) {
-        const int r = e / kTK, cc = e % kTK;
-        const int64_t j = j0 + r;
-        Bs[cc][r] = (j < L && t0 + cc < dim) ? p.rows[(row0 + j) * dim + t0 + cc] : 0.f;
-      }
+      __syncthreads();  // the previous slab's reads are done
+      st.store(As, Bs, tid);
       __syncthreads();
+      if (t0 + kTK < dim) st.fetch(p, s_q, row0, j0, L, t0 + kTK, tid);
+      // every score sums its products in k order: float4 reads along k, then the four steps
 #pragma unroll
-      for (int t = 0; t < kTK; ++t) {
-        float av[4], bv[4];
+      for (int t = 0; t < kTK; t += 4) {
+        float4 av[4], bv[4];
 #pragma unroll
-        for (int a = 0; a < 4; ++a) av[a] = As[t][ty + 16 * a];
+        for (int a = 0; a < 4; ++a)
+          av[a] = *reinterpret_cast<const float4*>(As + (ty + 16 * a) * kSlabStride + t);
 #pragma unroll
-        for (int b = 0; b < 4; ++b) bv[b] = Bs[t][tx + 16 * b];
+        for (int b = 0; b < 4; ++b)
+          bv[b] = *reinterpret_cast<const float4*>(Bs + (tx + 16 * b) * kSlabStride + t);
 #pragma unroll
         for (int a = 0; a < 4; ++a)
 #pragma unroll
-          for (int b = 0; b < 4; ++b) accumulate<ACC>(acc[a][b], cnt[a][b], av[a], bv[b]);
+          for (int b = 0; b < 4; ++b) {
+            accumulate<ACC>(acc[a][b], cnt[a][b], av[a].x, bv[b].x);
+            accumulate<ACC>(acc[a][b], cnt[a][b], av[a].y, bv[b].y);
+            accumulate<ACC>(acc[a][b], cnt[a][b], av[a].z, bv[b].z);
+            accumulate<ACC>(acc[a][b], cnt[a][b], av[a].w, bv[b].w);
+          }
       }
-      __syncthreads();
     }
     // scores (+inf for filtered rows, indexes.cpp:336-339)
 #pragma unroll
@@ -278,7 +353,7 @@ __global__ void __launch_bounds__(kThreads)
             const int src = __ffs(mask) - 1;
             mask &= mask - 1;
             const uint64_t x = __shfl_sync(0xffffffffu, key, src);
-            if (x < list[p.k_sel - 1]) warp_insert(list, p.k_sel, x, lane);
+            if (x < list[p.k_sel - 1]) insert_key(list, p.k_sel, x, lane);
           }
         }
       }
@@ -356,7 +431,7 @@ __global__ void ivf_emit_kernel(const __grid_constant__ IvfScanParams p,
         const int src = __ffs(mask) - 1;
         mask &= mask - 1;
         const uint64_t x = __shfl_sync(0xffffffffu, key, src);
-        if (x < list[K - 1]) warp_insert(list, K, x, lane);
+        if (x < list[K - 1]) insert_key(list, K, x, lane);
       }
     }
     best = list;
@@ -431,7 +506,7 @@ __global__ void coarse_select_kernel(const float* __restrict__ scores, int64_t r
       const int src = __ffs(mask) - 1;
       mask &= mask - 1;
       const uint64_t x = __shfl_sync(0xffffffffu, key, src);
-      if (x < list[K - 1]) warp_insert(list, K, x, lane);
+      if (x < list[K - 1]) insert_key(list, K, x, lane);
     }
   }
   for (int i = lane; i < K; i += 32) {
@@ -469,15 +544,21 @@ cudaError_t launch_scan(const IvfScanParams& p, int64_t grid, cudaStream_t strea
     kern<<<g, kThreads, dyn, stream>>>(p);
     return cudaGetLastError();
   };
+  const bool vec = p.dim % 4 == 0 && (reinterpret_cast<uintptr_t>(p.queries) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(p.rows) & 15) == 0;
   switch (acc_kind(p.metric)) {
     case kAccDot:
-      return run(ivf_scan_kernel<kAccDot, SORT>);
+      return vec ? run(ivf_scan_kernel<kAccDot, SORT, true>)
+                 : run(ivf_scan_kernel<kAccDot, SORT, false>);
     case kAccHamming:
-      return run(ivf_scan_kernel<kAccHamming, SORT>);
+      return vec ? run(ivf_scan_kernel<kAccHamming, SORT, true>)
+                 : run(ivf_scan_kernel<kAccHamming, SORT, false>);
     case kAccLp:
-      return run(ivf_scan_kernel<kAccLp, SORT>);
+      return vec ? run(ivf_scan_kernel<kAccLp, SORT, true>)
+                 : run(ivf_scan_kernel<kAccLp, SORT, false>);
     default:
-      return run(ivf_scan_kernel<kAccL2, SORT>);
+      return vec ? run(ivf_scan_kernel<kAccL2, SORT, true>)
+                 : run(ivf_scan_kernel<kAccL2, SORT, false>);
   }
 }
 
