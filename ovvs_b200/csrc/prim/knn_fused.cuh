@@ -19,8 +19,10 @@
 //   warps 0-7 epilogue     warps w, w+4 share TMEM lane quarter w % 4 (32 queries, one per
 //                          thread) and take columns [0,128) and [128,256): per 32
 //                          columns one tcgen05.ld and a 3-input max tree against the query's
-//                          current threshold. A lane whose chunk may hold a candidate (about 3%
-//                          of chunks) copies it to its private deferred row in shared memory;
+//                          current threshold. A lane whose chunk may hold a candidate (on
+//                          config 3: 0.14% of a lane's chunks; some lane of the warp in 2.9%
+//                          of a warp's chunks) copies it to its private deferred row in shared
+//                          memory;
 //                          the exact per-column checks + insertions into the thread's sorted
 //                          register list of the KL best (value, row id) keys run after the
 //                          TMEM buffer is handed back, so with 16 epilogue warps per pair tile
