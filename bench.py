@@ -480,8 +480,10 @@ def run_ours(args, cfg):
     res.synchronize()
 
     # ---- device-resident timing, phase events per launch --------------------------------
+    # The K searches are enqueued back to back (no host synchronisation between them, so a rank
+    # whose host is late does not hold up the others' all-gather); each search's phase events are
+    # kept by the library and read after the timed region.
     res.set_profiling(True)
-    phases = []
     barrier()
     with ClockSampler(local) as clocks:
         ev0 = torch.cuda.Event(enable_timing=True)
@@ -489,15 +491,22 @@ def run_ours(args, cfg):
         ev0.record(stream)
         for _ in range(args.steps):
             ix.search_device(dq, k, dn, dd)
-            phases.append(res.last_phase_ms())
         ev1.record(stream)
         ev1.synchronize()
         res.synchronize()
         barrier()
+    phases = res.phase_history(min(args.steps, 64))
     res.set_profiling(False)
     ms = max_over_ranks(ev0.elapsed_time(ev1))
     ms_step = ms / args.steps
     value = nq / (ms_step / 1e3)
+    # every rank's mean phases (prep, fused kernel, merge, cross-shard exchange): the exchange phase
+    # of a rank includes its wait for the slowest rank
+    rank_phases = [[round(statistics.mean(p[i] for p in phases), 4) for i in range(4)]]
+    if world > 1:
+        rank_phases = [None] * world
+        dist.all_gather_object(rank_phases, [round(statistics.mean(p[i] for p in phases), 4)
+                                             for i in range(4)])
 
     # ---- end to end through the C ABI with host buffers --------------------------------
     nb_h = np.empty(nq * k, np.int64)
@@ -558,6 +567,7 @@ def run_ours(args, cfg):
                 "build_s": round(build_s, 3),
                 "phase_ms_mean": [round(statistics.mean(p[i] for p in phases), 4)
                                   for i in range(4)],
+                **({"phase_ms_ranks": rank_phases} if world > 1 else {}),
             },
             "e2e": {"value": nq / (e2e_ms / 1e3), "unit": "queries/s",
                     "h2d_bytes_per_step": nq * dim * 4, "d2h_bytes_per_step": nq * k_eff * 12},

@@ -36,6 +36,14 @@ OVVS_API ovvsStatus ovvsResourcesDevice(ovvsResources_t res, int32_t* device);
 OVVS_API ovvsStatus ovvsResourcesSetProfiling(ovvsResources_t res, int32_t enable);
 OVVS_API ovvsStatus ovvsResourcesLastPhaseMs(ovvsResources_t res, float* ms, int32_t count);
 
+/* The same four phase durations for each of the last searches run while profiling was enabled (up
+   to 64, oldest first), so back-to-back searches can be timed without synchronising after each:
+   waits for the most recent one, writes min(recorded, max_searches) rows of 4 floats (ms) to `ms`
+   and their number to *count, then clears the record (enabling profiling also clears it). Not in
+   the reference. */
+OVVS_API ovvsStatus ovvsResourcesPhaseHistoryMs(ovvsResources_t res, float* ms,
+                                                int32_t max_searches, int32_t* count);
+
 /* ---- kernel watchdog ---------------------------------------------------------------------- */
 
 /* Every wait inside this library's kernels (on a copy, an MMA, another warp or another GPU) is

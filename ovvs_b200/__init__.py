@@ -114,6 +114,7 @@ def _bind(lib):
                                                c_void_p, c_void_p, c_void_p, c_void_p], c_int32),
         "ovvsResourcesSetProfiling": ([c_void_p, c_int32], c_int32),
         "ovvsResourcesLastPhaseMs": ([c_void_p, P(c_float), c_int32], c_int32),
+        "ovvsResourcesPhaseHistoryMs": ([c_void_p, P(c_float), c_int32, P(c_int32)], c_int32),
         "ovvsResourcesLastKernelError": ([c_void_p, P(c_int32)], c_int32),
         "ovvsWatchdogSelfTest": ([c_void_p, c_int64, P(c_int32)], c_int32),
         "ovvsNcclUniqueIdSize": ([], c_int32),
@@ -249,6 +250,15 @@ class Resources:
         ms = (c_float * 4)()
         _check(lib().ovvsResourcesLastPhaseMs(self._h, ms, 4), "phase times")
         return list(ms)
+
+    def phase_history(self, max_searches=64):
+        """The four phase times of each of the last searches run with profiling on (oldest first,
+        at most 64), read after they have all been enqueued back to back; clears the record."""
+        ms = (c_float * (4 * max_searches))()
+        n = c_int32()
+        _check(lib().ovvsResourcesPhaseHistoryMs(self._h, ms, max_searches, byref(n)),
+               "phase history")
+        return [list(ms[4 * i: 4 * i + 4]) for i in range(n.value)]
 
     # Primitives (reference python/ovvs/__init__.py Resources.gemm / topk / gather_rows, which
     # return flat lists; these return numpy arrays of the same values, shaped [rows, cols]).

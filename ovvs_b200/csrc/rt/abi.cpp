@@ -444,6 +444,32 @@ ovvsStatus ovvsResourcesSetProfiling(ovvsResources_t res, int32_t enable) {
   std::lock_guard<std::mutex> lk(r.mu);
   r.profiling = enable != 0;
   r.phase_valid = false;
+  r.hist_next = 0;
+  r.hist_count = 0;
+  return OVVS_STATUS_SUCCESS;
+}
+
+ovvsStatus ovvsResourcesPhaseHistoryMs(ovvsResources_t res, float* ms, int32_t max_searches,
+                                       int32_t* count) {
+  if (!res || !ms || !count || max_searches < 0) return OVVS_STATUS_INVALID_ARGUMENT;
+  Resources& r = *from_handle(res);
+  std::lock_guard<std::mutex> lk(r.mu);
+  const int n = std::min(r.hist_count, max_searches);
+  *count = 0;
+  if (n > 0) {
+    constexpr int H = Resources::kPhaseHistory;
+    OVVS_TRY_CUDA(cudaEventSynchronize(r.hist_ev[(r.hist_next - 1 + H) % H][Resources::kPhases]));
+    for (int s = 0; s < n; ++s) {
+      const int slot = (r.hist_next - n + s + H) % H;
+      for (int i = 0; i < Resources::kPhases; ++i) {
+        float v = 0.f;
+        OVVS_TRY_CUDA(cudaEventElapsedTime(&v, r.hist_ev[slot][i], r.hist_ev[slot][i + 1]));
+        ms[s * Resources::kPhases + i] = v;
+      }
+    }
+  }
+  *count = n;
+  r.hist_count = 0;
   return OVVS_STATUS_SUCCESS;
 }
 

@@ -96,6 +96,9 @@ Resources::~Resources() {
   if (d_err) cudaFree(d_err);
   for (auto& e : phase_ev)
     if (e) cudaEventDestroy(e);
+  for (auto& row : hist_ev)
+    for (auto& e : row)
+      if (e) cudaEventDestroy(e);
   if (stream) cudaStreamDestroy(stream);
 }
 
@@ -107,6 +110,16 @@ void Resources::mark(int i) {
   }
   cudaEventRecord(phase_ev[i], stream);
   phase_valid = true;
+  cudaEvent_t& h = hist_ev[hist_next][i];
+  if (!h && cudaEventCreate(&h) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return;
+  }
+  cudaEventRecord(h, stream);
+  if (i == kPhases) {
+    hist_next = (hist_next + 1) % kPhaseHistory;
+    if (hist_count < kPhaseHistory) ++hist_count;
+  }
 }
 
 ovvsStatus Resources::check_policy() const {

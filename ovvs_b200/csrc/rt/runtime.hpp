@@ -130,6 +130,12 @@ struct Resources {
   bool profiling = false;
   bool phase_valid = false;
   cudaEvent_t phase_ev[kPhases + 1] = {};
+  // While profiling, the phase boundaries of the last kPhaseHistory searches are also kept in a
+  // ring, so back-to-back searches can be timed without a synchronisation after each.
+  static constexpr int kPhaseHistory = 64;
+  cudaEvent_t hist_ev[kPhaseHistory][kPhases + 1] = {};
+  int hist_next = 0;   // ring slot of the search being recorded
+  int hist_count = 0;  // completed searches in the ring (<= kPhaseHistory)
   std::mutex mu;
   DeviceBuffer ws[kWsCount];
 

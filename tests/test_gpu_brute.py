@@ -301,3 +301,29 @@ def test_large_k_overflow_retry(ovvs, gpu, oracle):
     rnb, rds = oracle.brute_search(data, q, 100, "l2")
     assert_search_equal(nb, ds, rnb, rds, what="overflow retry")
     ix.close()
+
+
+def test_phase_history_of_back_to_back_searches(ovvs, gpu):
+    """Profiling keeps each search's phase times: three searches enqueued without a
+    synchronisation in between give three rows, the last one the last search's phases (recorded
+    by separate events at the same stream positions, so equal to within event resolution)."""
+    import torch
+
+    rng = np.random.default_rng(21)
+    ix = ovvs.BruteIndex.build(rng.standard_normal((20000, 64)).astype(np.float32),
+                               resources=gpu)
+    dq = torch.from_numpy(rng.standard_normal((300, 64)).astype(np.float32)).cuda()
+    dn = torch.empty((300, 10), dtype=torch.int64, device="cuda")
+    dd = torch.empty((300, 10), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    gpu.set_profiling(True)
+    for _ in range(3):
+        ix.search_device(dq, 10, dn, dd)
+    last = gpu.last_phase_ms()
+    hist = gpu.phase_history()
+    gpu.set_profiling(False)
+    assert len(hist) == 3
+    assert all(row[1] > 0.0 for row in hist)
+    assert np.allclose(hist[-1], last, rtol=0.05, atol=0.02)
+    assert gpu.phase_history() == []  # reading clears the record
+    ix.close()
