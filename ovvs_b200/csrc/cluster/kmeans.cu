@@ -62,29 +62,44 @@ __global__ void kmeans_bound_kernel(const float* __restrict__ x, const int64_t* 
 }
 
 // mixer.cpp:902-918: per centroid, fp32 sum of its rows in ascending row order, then
-// centroid = sum * (1 / count); a centroid without rows keeps its previous value.
+// centroid = sum * (1 / count); a centroid without rows keeps its previous value. One block per
+// centroid, one thread per dimension; the cluster's row ids are staged in shared memory 256 at a
+// time so that each thread keeps 8 independent row loads in flight (the additions stay in row
+// order).
+constexpr int kUpdateIdx = 256;
+
 __global__ void centroid_update_kernel(const float* __restrict__ x, int dim,
                                        const uint32_t* __restrict__ sorted_idx,
                                        const int* __restrict__ counts,
                                        const int* __restrict__ offsets,
                                        float* __restrict__ centroids) {
+  __shared__ uint32_t s_idx[kUpdateIdx];
   const int c = blockIdx.x;
   const int cnt = counts[c];
   if (cnt == 0) return;
   const int beg = offsets[c];
   const float inv = __fdiv_rn(1.f, static_cast<float>(cnt));
-  for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+  for (int d0 = 0; d0 < dim; d0 += blockDim.x) {
+    const int d = d0 + static_cast<int>(threadIdx.x);
     float s = 0.f;
-    int j = 0;
-    for (; j + 4 <= cnt; j += 4) {
-      const float v0 = x[static_cast<int64_t>(sorted_idx[beg + j]) * dim + d];
-      const float v1 = x[static_cast<int64_t>(sorted_idx[beg + j + 1]) * dim + d];
-      const float v2 = x[static_cast<int64_t>(sorted_idx[beg + j + 2]) * dim + d];
-      const float v3 = x[static_cast<int64_t>(sorted_idx[beg + j + 3]) * dim + d];
-      s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v0), v1), v2), v3);
+    for (int j0 = 0; j0 < cnt; j0 += kUpdateIdx) {
+      const int m = min(kUpdateIdx, cnt - j0);
+      __syncthreads();
+      for (int t = threadIdx.x; t < m; t += blockDim.x) s_idx[t] = sorted_idx[beg + j0 + t];
+      __syncthreads();
+      if (d < dim) {
+        int j = 0;
+        for (; j + 8 <= m; j += 8) {
+          float v[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) v[u] = x[static_cast<int64_t>(s_idx[j + u]) * dim + d];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) s = __fadd_rn(s, v[u]);
+        }
+        for (; j < m; ++j) s = __fadd_rn(s, x[static_cast<int64_t>(s_idx[j]) * dim + d]);
+      }
     }
-    for (; j < cnt; ++j) s = __fadd_rn(s, x[static_cast<int64_t>(sorted_idx[beg + j]) * dim + d]);
-    centroids[static_cast<int64_t>(c) * dim + d] = __fmul_rn(s, inv);
+    if (d < dim) centroids[static_cast<int64_t>(c) * dim + d] = __fmul_rn(s, inv);
   }
 }
 
