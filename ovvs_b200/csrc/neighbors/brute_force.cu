@@ -298,8 +298,12 @@ ovvsStatus search_large(rt::Resources& r, const BruteIndex& ix, const SearchCtx&
   OVVS_TRY_CUDA(cudaMemsetAsync(tau, 0xFF, static_cast<size_t>(c.q_pad) * sizeof(uint64_t), s));
 
   if (prepass) {
-    // Lists of 32 over every stride-th tile; the need-th smallest key of their union bounds the
-    // need-th best key of the whole database (the union holds real rows).
+    // Lists of kPreKL over every stride-th tile; the need-th smallest key of their union bounds
+    // the need-th best key of the whole database (the union holds real rows). Short lists keep
+    // the pre-pass cheap (each insertion walks the list): enough of them are used for the union
+    // to hold twice `need` keys, which still contains the sample's best `need`; longer lists only
+    // when 256 lists of 8 (or 16) cannot hold that many.
+    const int kPreKL = need <= 1024 ? 8 : (need <= 2048 ? 16 : 32);
     const int stride = ix.num_tiles >= 64 ? 8 : 1;
     const int sampled = (ix.num_tiles + stride - 1) / stride;
     prim::FusedParams p;
@@ -307,29 +311,29 @@ ovvsStatus search_large(rt::Resources& r, const BruteIndex& ix, const SearchCtx&
     p.tile_stride = stride;
     p.num_dbtiles = sampled;
     const int64_t cand_per_sc =
-        c.q_pad * 32 * prim::kListsPerItem * static_cast<int64_t>(sizeof(uint64_t));
+        c.q_pad * kPreKL * prim::kListsPerItem * static_cast<int64_t>(sizeof(uint64_t));
     int num_sc = choose_num_sc(c.num_qtiles, sampled, pair_sms(r, p), cand_per_sc, &p.tiles_per_item);
+    const int per_sc = kPreKL * prim::kListsPerItem;
     const int min_sc = static_cast<int>(
-        std::min<int64_t>(sampled, (2 * need + 32 * prim::kListsPerItem - 1) /
-                                       (32 * prim::kListsPerItem)));
+        std::min<int64_t>(sampled, (2 * need + per_sc - 1) / per_sc));
     if (num_sc < min_sc) {
       p.tiles_per_item = (sampled + min_sc - 1) / min_sc;
       num_sc = (sampled + p.tiles_per_item - 1) / p.tiles_per_item;
     }
     const int lists = num_sc * prim::kListsPerItem;
-    if (lists <= 256 && static_cast<int64_t>(lists) * 32 >= need) {
+    if (lists <= 256 && static_cast<int64_t>(lists) * kPreKL >= need) {
       p.num_sc = num_sc;
       p.num_items = prim::fused_items(c.num_qtiles, num_sc);
-      p.k_pub = 0;  // lists of 32 cannot bound rank `need`
+      p.k_pub = 0;  // short lists cannot bound rank `need`
       uint64_t* cand = nullptr;
       uint64_t* shared_bound = nullptr;
-      OVVS_TRY(r.scratch(rt::kWsCand, static_cast<size_t>(c.q_pad) * lists * 32, &cand));
+      OVVS_TRY(r.scratch(rt::kWsCand, static_cast<size_t>(c.q_pad) * lists * kPreKL, &cand));
       OVVS_TRY(r.scratch(rt::kWsAppBound, static_cast<size_t>(c.q_pad), &shared_bound));
       OVVS_TRY_CUDA(cudaMemsetAsync(shared_bound, 0xFF, static_cast<size_t>(c.q_pad) * 8, s));
       p.q_bound = shared_bound;
       p.out = cand;
-      OVVS_TRY_CUDA(prim::launch_knn_fused(c.maps, p, 32, launch_grid(p, pair_sms(r, p)), s));
-      OVVS_TRY_CUDA(prim::launch_kth_bound(cand, lists, nq, static_cast<int>(need), tau, s));
+      OVVS_TRY_CUDA(prim::launch_knn_fused(c.maps, p, kPreKL, launch_grid(p, pair_sms(r, p)), s));
+      OVVS_TRY_CUDA(prim::launch_kth_bound(cand, lists, nq, static_cast<int>(need), kPreKL, tau, s));
     }
   }
 

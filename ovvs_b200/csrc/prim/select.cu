@@ -298,8 +298,7 @@ __global__ void shard_merge_kernel(const float* __restrict__ rank, const int64_t
 }
 
 __global__ void kth_bound_kernel(const uint64_t* __restrict__ cand, int num_sc, int64_t nq,
-                                 int k, uint64_t* __restrict__ tau_key) {
-  constexpr int KL = 32;
+                                 int k, int KL, uint64_t* __restrict__ tau_key) {
   const int lane = threadIdx.x & 31;
   const int64_t q = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (q >= nq) return;
@@ -453,13 +452,13 @@ cudaError_t launch_merge_rerank(const MergeParams& p, cudaStream_t stream) {
   }
 }
 
-cudaError_t launch_kth_bound(const uint64_t* cand, int num_sc, int64_t nq, int k,
+cudaError_t launch_kth_bound(const uint64_t* cand, int num_sc, int64_t nq, int k, int kl,
                              uint64_t* tau_key, cudaStream_t stream) {
-  if (num_sc > 256) return cudaErrorInvalidValue;
+  if (num_sc > 256 || kl < 1) return cudaErrorInvalidValue;
   const int wpb = 8;
   const int64_t blocks = (nq + wpb - 1) / wpb;
   kth_bound_kernel<<<static_cast<unsigned>(blocks), wpb * 32, 0, stream>>>(cand, num_sc, nq, k,
-                                                                        tau_key);
+                                                                        kl, tau_key);
   return cudaGetLastError();
 }
 

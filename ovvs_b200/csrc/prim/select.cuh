@@ -47,10 +47,10 @@ struct MergeParams {
 
 cudaError_t launch_merge_rerank(const MergeParams& p, cudaStream_t stream);
 
-// Large k. tau_key[q] = the k-th smallest key of the union of the num_sc sorted lists of 32 keys
+// Large k. tau_key[q] = the k-th smallest key of the union of the num_sc sorted lists of kl keys
 // in cand (kEmptyKey when the union has fewer than k keys): an upper bound on the k-th best key
 // of the whole database, since the union holds real rows.
-cudaError_t launch_kth_bound(const uint64_t* cand, int num_sc, int64_t nq, int k,
+cudaError_t launch_kth_bound(const uint64_t* cand, int num_sc, int64_t nq, int k, int kl,
                              uint64_t* tau_key, cudaStream_t stream);
 
 // Large k. For each query the append buffer app_buf[q*cap, q*cap + min(count, cap)) is sorted,
