@@ -180,3 +180,33 @@ def test_argument_handling(ovvs, gpu, tmp_path):
     with pytest.raises(ovvs.OvvsError):
         ovvs.IvfFlatIndex.load(os.path.join(str(tmp_path), "missing.ivf"), dim=4, resources=gpu)
     ix.close()
+
+
+def test_device_search_unaligned_queries_and_odd_dim(ovvs, gpu, oracle, tmp_path):
+    """Device queries that are not 16-byte aligned, and a dim that is not a multiple of 4, take
+    the scan's scalar staging path; the results equal the oracle's."""
+    import torch
+
+    from oracle.cpu import read_ivf1
+
+    rng = np.random.default_rng(31)
+    for dim in (32, 30):
+        x = _mixture(rng, 6000, dim, 20)
+        q = _mixture(rng, 200, dim, 20)
+        ix = ovvs.IvfFlatIndex.build(x, 20, "l2", resources=gpu)
+        path = str(tmp_path / f"ix{dim}.ivf")
+        ix.save(path)
+        parts = read_ivf1(path)
+        rnb, rds = oracle.ivf_flat_search(x, "l2", parts["centroids"], parts["sizes"],
+                                          parts["ids"], q, 7, 4)
+        buf = torch.zeros(200 * dim + 1, dtype=torch.float32, device="cuda")
+        buf[1:].copy_(torch.from_numpy(q.ravel()))
+        dq = buf[1:].view(200, dim)  # starts 4 bytes into the allocation
+        assert dq.data_ptr() % 16 != 0
+        dn = torch.empty((200, 7), dtype=torch.int64, device="cuda")
+        dd = torch.empty((200, 7), dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()
+        ix.search_device(dq, 7, 4, dn, dd)
+        gpu.synchronize()
+        assert_search_equal(dn.cpu().numpy(), dd.cpu().numpy(), rnb, rds, what=f"dim {dim}")
+        ix.close()
