@@ -178,7 +178,7 @@ ovvsStatus fit(rt::Resources& r, const float* x, int64_t n_local, int64_t row_of
   }
   const size_t xbytes = static_cast<size_t>(n_local) * dim * sizeof(float);
   OVVS_TRY_CUDA(m.d_x.reserve(xbytes + 16));
-  OVVS_TRY_CUDA(cudaMemcpyAsync(m.d_x.get(), x, xbytes, cudaMemcpyHostToDevice, s));
+  OVVS_TRY(rt::upload(r, m.d_x.get(), x, xbytes));
   OVVS_TRY_CUDA(cudaStreamSynchronize(s));  // `init` is a host temporary
 
   const int64_t n = n_local;
@@ -296,8 +296,7 @@ ovvsStatus predict(rt::Resources& r, KMeansModel& m, const float* x, int64_t n, 
   OVVS_TRY(r.scratch(rt::kWsQueries, static_cast<size_t>(n) * m.dim, &dq));
   OVVS_TRY(r.scratch(rt::kWsNeighbors, static_cast<size_t>(n), &dl));
   OVVS_TRY(r.scratch(rt::kWsDistances, static_cast<size_t>(n), &dd));
-  OVVS_TRY_CUDA(cudaMemcpyAsync(dq, x, static_cast<size_t>(n) * m.dim * sizeof(float),
-                                cudaMemcpyHostToDevice, s));
+  OVVS_TRY(rt::upload(r, dq, x, static_cast<size_t>(n) * m.dim * sizeof(float)));
   int64_t k_eff = 0;
   OVVS_TRY(nb::search_device(r, m.index, dq, n, 1, nullptr, dl, dd, &k_eff));
   OVVS_TRY_CUDA(cudaMemcpyAsync(labels, dl, static_cast<size_t>(n) * sizeof(int64_t),

@@ -188,7 +188,7 @@ ovvsStatus build_from_host(rt::Resources& r, BruteIndex& ix, const void* data, i
   const size_t bytes = static_cast<size_t>(n) * dim * elem_size(dtype);
   rt::DeviceBuffer raw;
   OVVS_TRY_CUDA(raw.reserve(bytes));
-  OVVS_TRY_CUDA(cudaMemcpyAsync(raw.get(), data, bytes, cudaMemcpyHostToDevice, r.stream));
+  OVVS_TRY(rt::upload(r, raw.get(), data, bytes));
   ovvsStatus st = build_from_device(r, ix, raw.get(), dtype, n, dim, metric_raw, row_offset);
   if (st != OVVS_STATUS_SUCCESS) return st;
   ix.sharded = sharded && r.world > 1;

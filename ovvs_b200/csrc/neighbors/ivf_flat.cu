@@ -95,8 +95,7 @@ ovvsStatus build(rt::Resources& r, IvfFlatIndex& ix, const float* x, int64_t n, 
   }
   OVVS_TRY(set_centroids(r, ix));
   OVVS_TRY_CUDA(ix.d_x.reserve(bytes_of(n * dim, sizeof(float))));
-  OVVS_TRY_CUDA(cudaMemcpyAsync(ix.d_x.get(), x, n * dim * sizeof(float), cudaMemcpyHostToDevice,
-                                r.stream));
+  OVVS_TRY(rt::upload(r, ix.d_x.get(), x, n * dim * sizeof(float)));
   std::vector<int64_t> labels;
   OVVS_TRY(assign(r, ix, ix.d_x.as<float>(), n, labels));
   // build_ivf_lists (indexes.cpp:50-57): list c = rows labelled c, ascending.
@@ -125,8 +124,7 @@ ovvsStatus extend(rt::Resources& r, IvfFlatIndex& ix, const float* extra, int64_
     OVVS_TRY_CUDA(cudaMemcpyAsync(grown.get(), ix.d_x.get(), ix.n * ix.dim * sizeof(float),
                                   cudaMemcpyDeviceToDevice, s));
   float* dst = grown.as<float>() + ix.n * ix.dim;
-  OVVS_TRY_CUDA(cudaMemcpyAsync(dst, extra, nextra * ix.dim * sizeof(float),
-                                cudaMemcpyHostToDevice, s));
+  OVVS_TRY(rt::upload(r, dst, extra, nextra * ix.dim * sizeof(float)));
   std::vector<int64_t> labels(static_cast<size_t>(nextra), -1);
   if (ix.nlist > 0) OVVS_TRY(assign(r, ix, dst, nextra, labels));
   OVVS_TRY(r.finish());

@@ -1,10 +1,12 @@
 // CUDA runtime layer (see runtime.hpp).
 #include "runtime.hpp"
 
+#include <algorithm>
 #include <chrono>
 #include <cstdlib>
 #include <cstring>
 #include <thread>
+#include <vector>
 
 namespace ovvs {
 namespace rt {
@@ -99,6 +101,13 @@ Resources::~Resources() {
   for (auto& row : hist_ev)
     for (auto& e : row)
       if (e) cudaEventDestroy(e);
+  for (int b = 0; b < 2; ++b) {
+    if (stage_ev[b]) {
+      cudaEventSynchronize(stage_ev[b]);
+      cudaEventDestroy(stage_ev[b]);
+    }
+    if (stage_buf[b]) cudaFreeHost(stage_buf[b]);
+  }
   if (stream) cudaStreamDestroy(stream);
 }
 
@@ -202,6 +211,76 @@ ovvsStatus allreduce_i64_sum(Resources& r, int64_t* value) {
   OVVS_TRY(status_of(ovvs::rt::nccl()->AllReduce(d, d, 1, ncclInt64, ncclSum, r.comm, r.stream)));
   OVVS_TRY_CUDA(cudaMemcpyAsync(value, d, sizeof(int64_t), cudaMemcpyDeviceToHost, r.stream));
   OVVS_TRY_CUDA(cudaStreamSynchronize(r.stream));
+  return OVVS_STATUS_SUCCESS;
+}
+
+namespace {
+
+constexpr size_t kStageMin = size_t(16) << 20;    // smaller copies go direct
+constexpr size_t kStageChunk = size_t(32) << 20;  // bytes per staging buffer
+
+// memcpy split over `threads` host threads.
+void parallel_copy(void* dst, const void* src, size_t bytes, unsigned threads) {
+  if (threads <= 1 || bytes < (size_t(1) << 20)) {
+    std::memcpy(dst, src, bytes);
+    return;
+  }
+  std::vector<std::thread> pool;
+  const size_t part = (bytes + threads - 1) / threads;
+  for (unsigned t = 0; t < threads; ++t) {
+    const size_t lo = t * part;
+    if (lo >= bytes) break;
+    const size_t len = std::min(part, bytes - lo);
+    pool.emplace_back([=] {
+      std::memcpy(static_cast<char*>(dst) + lo, static_cast<const char*>(src) + lo, len);
+    });
+  }
+  for (auto& th : pool) th.join();
+}
+
+}  // namespace
+
+ovvsStatus upload(Resources& r, void* dst, const void* src, size_t bytes) {
+  if (bytes == 0) return OVVS_STATUS_SUCCESS;
+  bool direct = bytes < kStageMin;
+  if (!direct) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, src) == cudaSuccess && a.type == cudaMemoryTypeHost)
+      direct = true;  // already pinned (or registered): the DMA reads it directly
+    (void)cudaGetLastError();
+  }
+  if (!direct) {
+    for (int b = 0; b < 2 && !direct; ++b) {
+      if (!r.stage_buf[b] && cudaMallocHost(&r.stage_buf[b], kStageChunk) != cudaSuccess) {
+        r.stage_buf[b] = nullptr;
+        direct = true;  // no pinned memory to spare: the driver's pageable path
+      }
+      if (!direct && !r.stage_ev[b] &&
+          cudaEventCreateWithFlags(&r.stage_ev[b], cudaEventDisableTiming) != cudaSuccess) {
+        r.stage_ev[b] = nullptr;
+        direct = true;
+      }
+    }
+    (void)cudaGetLastError();
+  }
+  if (direct) {
+    OVVS_TRY_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, r.stream));
+    return OVVS_STATUS_SUCCESS;
+  }
+  const unsigned threads = std::max(1u, std::min(8u, std::thread::hardware_concurrency() / 2));
+  size_t off = 0;
+  for (int i = 0; off < bytes; ++i) {
+    const int b = i & 1;
+    const size_t len = std::min(kStageChunk, bytes - off);
+    // the DMA that last read this buffer has finished before it is refilled
+    if (r.stage_used[b]) OVVS_TRY_CUDA(cudaEventSynchronize(r.stage_ev[b]));
+    parallel_copy(r.stage_buf[b], static_cast<const char*>(src) + off, len, threads);
+    OVVS_TRY_CUDA(cudaMemcpyAsync(static_cast<char*>(dst) + off, r.stage_buf[b], len,
+                                  cudaMemcpyHostToDevice, r.stream));
+    OVVS_TRY_CUDA(cudaEventRecord(r.stage_ev[b], r.stream));
+    r.stage_used[b] = true;
+    off += len;
+  }
   return OVVS_STATUS_SUCCESS;
 }
 

@@ -138,6 +138,10 @@ struct Resources {
   int hist_count = 0;  // completed searches in the ring (<= kPhaseHistory)
   std::mutex mu;
   DeviceBuffer ws[kWsCount];
+  // Pinned staging buffers of upload() (allocated on the first large upload).
+  void* stage_buf[2] = {};
+  cudaEvent_t stage_ev[2] = {};
+  bool stage_used[2] = {};
 
   ~Resources();
   // Makes `device` current on the calling thread and creates the stream / error word on first
@@ -170,6 +174,12 @@ void probe_device(Resources& r, int device);
 // the swizzle that matches box_cols * 2 bytes (128/64/32).
 bool encode_f16_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows,
                    uint32_t box_cols, uint32_t box_rows);
+
+// Enqueues a host -> device copy of `bytes` on r.stream; the host buffer may be reused as soon as
+// this returns (as with a pageable cudaMemcpyAsync). Large pageable buffers go through two pinned
+// staging buffers filled by several host threads while the previous chunk's DMA runs, which is
+// faster than the driver's own pageable path; small or already pinned buffers are copied directly.
+ovvsStatus upload(Resources& r, void* dst, const void* src, size_t bytes);
 
 // Global row count of a sharded dataset (sum over ranks) and other small all-reduces.
 ovvsStatus allreduce_i64_sum(Resources& r, int64_t* value);
