@@ -103,19 +103,38 @@ __global__ void centroid_update_kernel(const float* __restrict__ x, int dim,
   }
 }
 
-// Sharded variant: this shard's per-centroid sums in fp64 (all-reduced afterwards).
+// Sharded variant: this shard's per-centroid sums in fp64 (all-reduced afterwards), with the
+// cluster's row ids staged in shared memory like centroid_update_kernel.
 __global__ void centroid_partial_kernel(const float* __restrict__ x, int dim,
                                         const uint32_t* __restrict__ sorted_idx,
                                         const int* __restrict__ counts,
                                         const int* __restrict__ offsets,
                                         double* __restrict__ sum64, double* __restrict__ cnt64) {
+  __shared__ uint32_t s_idx[kUpdateIdx];
   const int c = blockIdx.x;
   const int cnt = counts[c];
   const int beg = offsets[c];
-  for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+  for (int d0 = 0; d0 < dim; d0 += blockDim.x) {
+    const int d = d0 + static_cast<int>(threadIdx.x);
     double s = 0.0;
-    for (int j = 0; j < cnt; ++j) s += x[static_cast<int64_t>(sorted_idx[beg + j]) * dim + d];
-    sum64[static_cast<int64_t>(c) * dim + d] = s;
+    for (int j0 = 0; j0 < cnt; j0 += kUpdateIdx) {
+      const int m = min(kUpdateIdx, cnt - j0);
+      __syncthreads();
+      for (int t = threadIdx.x; t < m; t += blockDim.x) s_idx[t] = sorted_idx[beg + j0 + t];
+      __syncthreads();
+      if (d < dim) {
+        int j = 0;
+        for (; j + 8 <= m; j += 8) {
+          float v[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) v[u] = x[static_cast<int64_t>(s_idx[j + u]) * dim + d];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) s += v[u];
+        }
+        for (; j < m; ++j) s += x[static_cast<int64_t>(s_idx[j]) * dim + d];
+      }
+    }
+    if (d < dim) sum64[static_cast<int64_t>(c) * dim + d] = s;
   }
   if (threadIdx.x == 0) cnt64[c] = static_cast<double>(cnt);
 }
