@@ -1,0 +1,73 @@
+"""Host-side logic of bench.py that the round-end measurements rely on (no GPU needed)."""
+
+import os
+
+import numpy as np
+
+import bench
+
+
+def test_clock_summary_median_max_and_reasons():
+    cs = bench.ClockSampler(0)
+    cs.lines = [
+        "1965, 1965, 0, Not Active, Not Active, Not Active, Not Active",
+        "1700, 1965, 0, Not Active, Not Active, Not Active, Active",
+        "1710, 1965, 0, Active, Not Active, Not Active, Active",
+        "not a sample",
+    ]
+    s = cs.summary()
+    assert s["samples"] == 3
+    assert s["sm_mhz"] == 1710.0
+    assert s["sm_max_mhz"] == 1965.0
+    assert s["reasons"] == ["hw_slowdown", "sw_power_cap"]
+
+
+def test_clock_summary_without_samples():
+    s = bench.ClockSampler(0).summary()
+    assert s["sm_mhz"] is None and s["samples"] == 0 and s["reasons"] == []
+
+
+def test_search_launch_counts():
+    # small k: query prep, fused kernel, merge + re-rank (+ cross-shard merge when sharded)
+    assert bench._search_launches(10, 10_000_000, 1) == 3
+    assert bench._search_launches(10, 1_250_000, 8) == 4
+    # k = 100 (need 113 > 32): prep, bound pre-pass, k-th bound, append pass, select + re-rank
+    assert bench._search_launches(100, 1_000_000, 1) == 5
+    # no pre-pass at or below 4,096 rows
+    assert bench._search_launches(100, 3_000, 1) == 3
+    # k = 28 still fits the register lists (need 28 + 4 = 32)
+    assert bench._search_launches(28, 1_000_000, 1) == 3
+
+
+def test_metric_names():
+    assert bench.metric_name(bench.CONFIGS["c3"]) == bench.METRIC_NAME
+    assert "N=100M D=96 f16 inner_product k=100" in bench.metric_name(bench.CONFIGS["c5"])
+    assert "N=100k" in bench.metric_name(bench.CONFIGS["c1"])
+
+
+def test_traffic_figures_come_from_the_committed_profile():
+    assert bench._traffic_from_profiles("c3s") == 821530624.0
+    assert bench._traffic_from_profiles("c3") == 5 * 821530624.0
+    assert bench._traffic_from_profiles("no-such-config") is None
+
+
+def test_ivf_file_lists_reads_the_reference_format(tmp_path):
+    from oracle.cpu import write_ivf1
+
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((50, 6)).astype(np.float32)
+    cents = rng.standard_normal((4, 6)).astype(np.float32)
+    sizes = np.array([10, 0, 25, 15], np.int64)
+    ids = rng.permutation(50).astype(np.int64)
+    path = os.path.join(str(tmp_path), "ix.ivf")
+    write_ivf1(path, x, cents, sizes, ids, 0)
+    got_c, got_sizes = bench._ivf_file_lists(path)
+    assert np.array_equal(got_c, cents)
+    assert np.array_equal(got_sizes, sizes)
+
+
+def test_reference_sample_sizes_are_bounded():
+    threads, nq = bench._ivf_reference_sizes(bench.CONFIGS["ivf"], 12.0)
+    assert threads >= 1 and threads <= nq <= bench.CONFIGS["ivf"]["nq"]
+    rows = bench._reference_kmeans_rows(bench.CONFIGS["c4"], 12.0)
+    assert bench.CONFIGS["c4"]["clusters"] <= rows <= bench.CONFIGS["c4"]["n"]
