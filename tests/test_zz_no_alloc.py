@@ -8,8 +8,6 @@ fixed scratch array. This file is collected last so that a failure here stops a 
 after every other test has run; it also passes alone in a fresh process.
 """
 
-import ctypes
-
 import numpy as np
 import pytest
 
