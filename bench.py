@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the ovvs brute-force kNN path on B200.
 
-Workload (default, BASELINE.json metric "kNN queries/sec @ N=10M D=128 fp16 k=10"): config 3 --
+Workload (default; the headline metric "kNN queries/sec @ N=10M D=128 fp16 k=10"): config 3 --
 L2 kNN over N=10,000,000 x 128 fp16 rows drawn from a Gaussian mixture of 1,024 centres
 (centres ~ N(0, 4I), rows = centre + N(0, I)), Q=10,000 queries from the same mixture rounded to
 fp16, k=10, seed 2. Data is synthetic and generated on the GPU with torch's seeded CUDA RNG in
@@ -80,7 +80,7 @@ METRIC_NAME = "kNN queries/sec @ N=10M D=128 fp16 k=10 at 1/2/4/8 B200; % of roo
 
 
 def metric_name(cfg):
-    """BASELINE's metric for config 3; the same quantity named with its own shape for the other
+    """The headline metric for config 3; the same quantity named with its own shape for the other
     kNN configs (their lines are measurements of those configs, not of the headline)."""
     if cfg is CONFIGS["c3"]:
         return METRIC_NAME

@@ -3,7 +3,7 @@
 Expected: neighbour ids identical to the reference, distances bit-identical (the merge kernel
 re-evaluates each selected pair with the reference's own fp32 operation order). The only allowed
 difference is a near-tie at the cut-off, where another row whose exact distance is within the
-BASELINE tolerance (fp32 1e-4, fp16 2e-3 relative) may be returned instead.
+parity tolerance (fp32 1e-4, fp16 2e-3 relative) may be returned instead.
 """
 
 import os
@@ -139,7 +139,7 @@ def test_list_sizes(k, ovvs, gpu, oracle):
 
 
 def test_uniform_c1_shape_full(ovvs, gpu, oracle):
-    """BASELINE config 1 at full size: L2 fp32, N=100k x 128 Uniform[0,1), Q=1000, k=10."""
+    """Config 1 at full size: L2 fp32, N=100k x 128 Uniform[0,1), Q=1000, k=10."""
     _run_parity(ovvs, gpu, oracle, "l2", "f32", n=100_000, dim=128, nq=1000, k=10, seed=0,
                 kind="uniform")
 
