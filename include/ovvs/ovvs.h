@@ -7,8 +7,10 @@
  * libovvs.so in place of the reference one without recompiling.
  *
  * What runs on the GPU: the exact brute-force kNN path (build, typed build, search, destroy),
- * the allow-list bitset helper, k-means fit/predict/centroids/destroy, the dynamic batcher on top
- * of brute-force search, and the Resources/status/version plumbing. Every other entry point is
+ * the allow-list bitset helper, k-means fit/predict/centroids/destroy, IVF-Flat (build, search,
+ * serialize, deserialize, extend, destroy), the dynamic batcher on top of brute-force search,
+ * the dense primitives and all-neighbors, and the Resources/status/version plumbing. Every other
+ * entry point is
  * exported so that existing binaries still link and `import ovvs` still succeeds, and returns
  * OVVS_STATUS_UNSUPPORTED (see the "Outside this library's scope" section). There is no CPU
  * fallback: without a usable B200 the hot path returns OVVS_STATUS_DEVICE_UNAVAILABLE.
@@ -321,9 +323,15 @@ OVVS_API ovvsStatus ovvsBruteForceSearch(ovvsResources_t res, ovvsBruteForceInde
 OVVS_API ovvsStatus ovvsBruteForceDestroy(ovvsBruteForceIndex_t index);
 
 /* ------------------------------------------------------------------------------------------ */
-/* Outside this library's scope: exported, return OVVS_STATUS_UNSUPPORTED.                      */
+/* IVF-Flat  (reference src/neighbors/indexes.cpp:281-457)                                      */
 /* ------------------------------------------------------------------------------------------ */
 
+/* Build: nlist = min(nlist, n) lists from a 12-iteration k-means fit (squared L2) and each row's
+   nearest centroid; the dataset is copied. Search: per query the nprobe nearest lists (nprobe
+   clamped to [1, nlist]) are scored exactly with the index metric; neighbors/distances are host
+   [nq x k], ties go to the earlier row in probe order, and -1 / +inf fill the rows past a query's
+   candidates. Serialize/Deserialize use the reference's 'IVF1' file format. Extend appends rows
+   (ids n, n+1, ...) to the lists of their nearest centroids. */
 OVVS_API ovvsStatus ovvsIvfFlatBuild(ovvsResources_t res, const float* dataset, int64_t n,
                                      int64_t dim, ovvsMetric metric, int32_t nlist,
                                      ovvsIvfFlatIndex_t* index);
@@ -337,6 +345,10 @@ OVVS_API ovvsStatus ovvsIvfFlatDeserialize(ovvsResources_t res, const char* path
 OVVS_API ovvsStatus ovvsIvfFlatExtend(ovvsResources_t res, ovvsIvfFlatIndex_t index,
                                       const float* extra, int64_t nextra);
 OVVS_API ovvsStatus ovvsIvfFlatDestroy(ovvsIvfFlatIndex_t index);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Outside this library's scope: exported, return OVVS_STATUS_UNSUPPORTED.                      */
+/* ------------------------------------------------------------------------------------------ */
 
 OVVS_API ovvsStatus ovvsIvfPqBuild(ovvsResources_t res, const float* dataset, int64_t n,
                                    int64_t dim, ovvsMetric metric, int32_t nlist, int32_t pq_m,
