@@ -126,3 +126,18 @@ def test_ivf_flat_cases_bit_exact(golden_ivf, oracle):
         nb, ds = oracle.ivf_flat_search(x, int(c["metric"]), cents, sizes, ids, c["queries"],
                                         int(c["k"]), int(c["nprobe"]), bits)
         assert_search_equal(nb, ds, c["neighbors"], c["distances"], what=name)
+
+
+def test_ivf_flat_probing_every_list_is_brute_force(oracle):
+    """With nprobe = nlist every row is a candidate, so the IVF-Flat search returns the brute-force
+    distances (ids agree except between rows of equal distance: IVF breaks those ties by probe
+    position, brute force by row id)."""
+    rng = np.random.default_rng(12)
+    x = rng.standard_normal((2000, 16)).astype(np.float32)
+    q = rng.standard_normal((40, 16)).astype(np.float32)
+    cents, sizes, ids = oracle.ivf_flat_build(x, 12)
+    for metric in ("l2", "inner_product", "cosine"):
+        nb, ds = oracle.ivf_flat_search(x, metric, cents, sizes, ids, q, 9, cents.shape[0])
+        bnb, bds = oracle.brute_search(x, q, 9, metric)
+        assert np.all(same_bits(ds.ravel(), bds)), metric
+        assert np.mean(nb.ravel() == bnb) > 0.99, metric
