@@ -6,8 +6,10 @@ CPU-baseline / reference arm. The product package (``ovvs_b200``) never imports 
 Two checkers are exposed:
 
 * :class:`Oracle` -- ``liboracle.so``, this repository's restatement of the reference's
-  brute-force / k-means arithmetic (oracle/ovvs_oracle.cpp), bit-identical to the reference's
-  FORCE_CPU path.
+  brute-force / k-means / IVF-Flat arithmetic (oracle/ovvs_oracle.cpp), bit-identical to the
+  reference's FORCE_CPU path.
+
+``read_ivf1`` / ``write_ivf1`` read and write index files in the reference's IVF-Flat format.
 * :class:`Reference` -- ``libovvs_ref.so``, the reference library itself compiled from its own
   sources by oracle/Makefile (present when the reference checkout was available at build time).
 """

@@ -1,5 +1,5 @@
 #pragma once
-/* CPU restatement of the reference's brute-force kNN and k-means path.
+/* CPU restatement of the reference's brute-force kNN, k-means and IVF-Flat path.
  *
  * TEST INFRASTRUCTURE ONLY. This is the checker the GPU library is compared against; the product
  * (libovvs.so) never links, loads or calls it. Every function follows the reference's arithmetic
