@@ -8,8 +8,9 @@ import numpy as np
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-# The reference checkout (read only by the CPU tests that compare against it; they skip without it)
-REF_DIR = os.environ.get("REF_DIR", "/root/reference")
+# The reference checkout: REF_DIR, else `reference` beside this repository (read only by the CPU
+# tests that compare against it; they skip without it)
+REF_DIR = os.environ.get("REF_DIR") or os.path.join(os.path.dirname(ROOT), "reference")
 
 def _declared_symbols():
     names = set()
