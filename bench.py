@@ -279,10 +279,62 @@ def _traffic_from_profiles(config_name):
 # ---------------------------------------------------------------------------------------------
 # the reference CPU path (oracle/_ref/libovvs_ref.so, the reference built from its sources)
 # ---------------------------------------------------------------------------------------------
+def _order_key(v):
+    """uint32 image of float32 scores in the reference's top-k order (cpu_prims.cpp:24-32):
+    numbers ascending, -0 equal to +0, NaN after every number."""
+    v = np.asarray(v, np.float32)
+    u = v.view(np.uint32).copy()
+    u[v == 0] = 0
+    key = np.where(u & 0x80000000, ~u, u | 0x80000000).astype(np.uint32)
+    key[np.isnan(v)] = 0xFFFFFFFF
+    return key
+
+
+def _merge_shard_topk(parts, k_eff, inner_product):
+    """Merges per-shard top-k lists [(nb [nq, ks] global ids, ds [nq, ks])] into the top k_eff of
+    their union, ordered like the reference's cpu_topk: score (for inner product the score is the
+    negated distance it reports), then lower global id. Exact: every score depends only on its
+    (query, row) pair and the order is strict."""
+    nb = np.concatenate([p[0] for p in parts], axis=1)
+    ds = np.concatenate([p[1] for p in parts], axis=1)
+    score = -ds if inner_product else ds
+    key = _order_key(score)
+    out_nb = np.empty((nb.shape[0], k_eff), np.int64)
+    out_ds = np.empty((nb.shape[0], k_eff), np.float32)
+    for q in range(nb.shape[0]):
+        o = np.lexsort((nb[q], key[q]))[:k_eff]
+        out_nb[q] = nb[q, o]
+        out_ds[q] = ds[q, o]
+    return out_nb, out_ds
+
+
+def _parity(nb, ds, nb_ref, ds_ref, rtol):
+    """Parity of this library's results with the reference's on the same queries: ids equal, and
+    where they differ the two distances at that rank within `rtol` (a near-tie at the cut-off);
+    distances bit-identical where ids agree."""
+    nb, ds = np.asarray(nb), np.asarray(ds, np.float32)
+    same = nb == nb_ref
+    both_nan = np.isnan(ds) & np.isnan(ds_ref)
+    bits = (ds.view(np.uint32) == ds_ref.view(np.uint32)) | both_nan
+    with np.errstate(invalid="ignore", divide="ignore"):
+        rel = np.abs(ds.astype(np.float64) - ds_ref) / np.maximum(np.abs(ds_ref.astype(np.float64)),
+                                                                   1e-30)
+    rel[both_nan | (ds == ds_ref)] = 0.0
+    ties = ~same & (rel <= rtol)
+    out = {"queries": int(nb.shape[0]), "positions": int(nb.size),
+           "id_mismatch": int((~same).sum()), "id_mismatch_beyond_tie": int((~same & ~ties).sum()),
+           "distance_bits_differ_where_ids_agree": int((same & ~bits).sum()),
+           "max_rel_err": float(rel.max()) if rel.size else 0.0, "rtol": rtol}
+    out["ok"] = out["id_mismatch_beyond_tie"] == 0 and out["distance_bits_differ_where_ids_agree"] == 0
+    return out
+
+
 def _reference_sample(cfg, data_host, q_host, threads, n_queries):
     """Times the reference's FORCE_CPU ovvsBruteForceSearch on `n_queries` queries against all
     rows: row shards of 1M, `threads` host threads per shard (one Resources each, sharing the
-    shard's immutable index as the reference allows). Returns (seconds, shard top-k results)."""
+    shard's immutable index as the reference allows). Returns (seconds, neighbours, distances):
+    the shards' top-k lists merged into the reference's answer over all rows (the merge is not
+    timed)."""
     import ctypes
 
     from oracle.cpu import DTYPES, METRICS, Reference
@@ -294,8 +346,12 @@ def _reference_sample(cfg, data_host, q_host, threads, n_queries):
     per = [np.array_split(np.arange(n_queries), threads)[t] for t in range(threads)]
     res = [ref.resources() for _ in range(threads)]
     total = 0.0
+    parts = []
     for s0 in range(0, cfg["n"], CHUNK):
         shard = np.ascontiguousarray(data_host[s0: s0 + CHUNK])
+        ks = min(k, shard.shape[0])
+        part_nb = np.empty((n_queries, ks), np.int64)
+        part_ds = np.empty((n_queries, ks), np.float32)
         ix = ctypes.c_void_p()
         assert L.ovvsBruteForceBuildTyped(res[0], shard.ctypes.data_as(ctypes.c_void_p),
                                           shard.shape[0], shard.shape[1], METRICS[cfg["metric"]],
@@ -313,6 +369,8 @@ def _reference_sample(cfg, data_host, q_host, threads, n_queries):
                                         nb.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)),
                                         ds.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
             assert st == 0
+            part_nb[idx] = nb[: idx.size * ks].reshape(idx.size, ks) + s0
+            part_ds[idx] = ds[: idx.size * ks].reshape(idx.size, ks)
 
         th = [threading.Thread(target=work, args=(t,)) for t in range(threads)]
         t0 = time.perf_counter()
@@ -322,9 +380,11 @@ def _reference_sample(cfg, data_host, q_host, threads, n_queries):
             x.join()
         total += time.perf_counter() - t0
         L.ovvsBruteForceDestroy(ix)
+        parts.append((part_nb, part_ds))
     for r in res:
         L.ovvsResourcesDestroy(r)
-    return total
+    nb, ds = _merge_shard_topk(parts, min(k, cfg["n"]), cfg["metric"] == "inner_product")
+    return total, nb, ds
 
 
 def _reference_sizes(cfg, seconds):
@@ -403,7 +463,7 @@ def run_reference_arm(args, cfg):
     threads, nq = _reference_sizes(cfg, args.ref_seconds)
     for _ in range(args.warmup):
         _reference_sample(cfg, data_host, q_host, threads, threads)
-    secs = [_reference_sample(cfg, data_host, q_host, threads, nq) for _ in range(args.steps)]
+    secs = [_reference_sample(cfg, data_host, q_host, threads, nq)[0] for _ in range(args.steps)]
     t = sum(secs)
     value = nq * args.steps / t
     line = {
@@ -595,13 +655,22 @@ def run_ours(args, cfg):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads, nq_s = _reference_sizes(cfg, args.ref_seconds)
         data_host = shard_host
-        secs = _reference_sample(cfg, data_host, q_host, threads, nq_s)
+        secs, nb_ref, ds_ref = _reference_sample(cfg, data_host, q_host, threads, nq_s)
         line["cpu_baseline"] = {
             "value": nq_s / secs, "unit": "queries/s", "cores": threads, "kind": "reference",
             "sample": f"{nq_s} queries x all {n} rows: the reference library built from its "
                       f"sources (oracle/_ref), FORCE_CPU, 1M-row shards, {threads} threads"}
+        # The same sampled queries' results from the timed runs above, against the reference's.
+        parity = _parity(nb_h[: nq_s * k_eff].reshape(nq_s, k_eff),
+                         ds_h[: nq_s * k_eff].reshape(nq_s, k_eff), nb_ref, ds_ref,
+                         2e-3 if cfg["dtype"] == "f16" else 1e-4)
+        parity["against"] = "the reference library (oracle/_ref), FORCE_CPU, same queries"
+        line["parity"] = parity
     if rank == 0:
         print(json.dumps(line), flush=True)
+        if "parity" in line and not line["parity"]["ok"]:
+            print("parity FAILED against the reference", file=sys.stderr)
+            return 1
     return 0
 
 

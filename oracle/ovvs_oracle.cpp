@@ -249,9 +249,88 @@ void oracle_topk(const float* scores, int64_t rows, int64_t cols, int64_t k, int
   topk_rows(scores, rows, cols, k, indices, values, largest != 0);
 }
 
+namespace {
+
+/* Few queries against many rows: each thread takes a contiguous row shard, selects every query's
+   top min(k, shard rows) there with the reference's arithmetic and total order (cpu_prims.cpp:
+   24-32), and the shard lists are merged by the same order on (value, global id). Every score
+   depends only on its (query, row) pair and the order is strict, so the result equals the
+   unsharded brute_search_impl (mixer.cpp:843-864) bit for bit. */
+void brute_search_row_sharded(const float* data, int64_t n, int64_t dim, int32_t metric,
+                              const float* queries, int64_t nq, int64_t k, const uint8_t* bitset,
+                              int64_t* neighbors, float* distances, int32_t nthreads) {
+  const int64_t shards = std::max<int64_t>(1, std::min<int64_t>(nthreads, n / 16384));
+  const int64_t k_eff = std::min(k, n);
+  const float inf = std::numeric_limits<float>::infinity();
+  std::vector<std::vector<int64_t>> sid(static_cast<size_t>(shards));
+  std::vector<std::vector<float>> sval(static_cast<size_t>(shards));
+  std::vector<int64_t> lo(static_cast<size_t>(shards) + 1);
+  for (int64_t t = 0; t <= shards; ++t) lo[static_cast<size_t>(t)] = n * t / shards;
+  parallel_for(shards, static_cast<int32_t>(shards), [&](int64_t t0, int64_t t1) {
+    for (int64_t t = t0; t < t1; ++t) {
+      const int64_t b = lo[static_cast<size_t>(t)], rows = lo[static_cast<size_t>(t) + 1] - b;
+      const int64_t ks = std::min(k, rows);
+      std::vector<float> ynorm(static_cast<size_t>(rows));
+      for (int64_t j = 0; j < rows; ++j)
+        ynorm[static_cast<size_t>(j)] = nrm2sq_seq(data + (b + j) * dim, dim);
+      auto& ids = sid[static_cast<size_t>(t)];
+      auto& vals = sval[static_cast<size_t>(t)];
+      ids.resize(static_cast<size_t>(nq * ks));
+      vals.resize(static_cast<size_t>(nq * ks));
+      const int64_t block = 16;
+      std::vector<float> scores(static_cast<size_t>(block * rows));
+      for (int64_t q0 = 0; q0 < nq; q0 += block) {
+        const int64_t m = std::min(block, nq - q0);
+        pairwise_block(metric, queries + q0 * dim, m, data + b * dim, rows, dim, ynorm.data(),
+                       scores.data(), 2.f);
+        if (bitset) {
+          for (int64_t i = 0; i < m; ++i)
+            for (int64_t j = 0; j < rows; ++j) {
+              const int64_t g = b + j;
+              if (!((bitset[g >> 3] >> (g & 7)) & 1u)) scores[static_cast<size_t>(i * rows + j)] = inf;
+            }
+        }
+        topk_rows(scores.data(), m, rows, k, ids.data() + q0 * ks, vals.data() + q0 * ks, false);
+      }
+      for (auto& v : ids) v += b;
+    }
+  });
+  parallel_for(nq, nthreads, [&](int64_t q0, int64_t q1) {
+    std::vector<std::pair<float, int64_t>> all;
+    for (int64_t q = q0; q < q1; ++q) {
+      all.clear();
+      for (int64_t t = 0; t < shards; ++t) {
+        const int64_t rows = lo[static_cast<size_t>(t) + 1] - lo[static_cast<size_t>(t)];
+        const int64_t ks = std::min(k, rows);
+        for (int64_t i = 0; i < ks; ++i)
+          all.emplace_back(sval[static_cast<size_t>(t)][static_cast<size_t>(q * ks + i)],
+                           sid[static_cast<size_t>(t)][static_cast<size_t>(q * ks + i)]);
+      }
+      std::partial_sort(all.begin(), all.begin() + k_eff, all.end(),
+                        [](const std::pair<float, int64_t>& x, const std::pair<float, int64_t>& y) {
+                          return before(x.first, x.second, y.first, y.second, false);
+                        });
+      for (int64_t i = 0; i < k_eff; ++i) {
+        neighbors[q * k_eff + i] = all[static_cast<size_t>(i)].second;
+        distances[q * k_eff + i] = all[static_cast<size_t>(i)].first;
+      }
+    }
+  });
+}
+
+}  // namespace
+
 void oracle_brute_search(const float* data, int64_t n, int64_t dim, int32_t metric,
                          const float* queries, int64_t nq, int64_t k, const uint8_t* bitset,
                          int64_t* neighbors, float* distances, int32_t nthreads) {
+  if (nthreads > 1 && nq < 4 * static_cast<int64_t>(nthreads) && n >= 2 * 16384) {
+    brute_search_row_sharded(data, n, dim, metric, queries, nq, k, bitset, neighbors, distances,
+                             nthreads);
+    /* mixer.cpp:860-862: negation covers nq*k entries (k as requested, not min(k, n)). */
+    if (metric == kIP)
+      for (int64_t i = 0; i < nq * k; ++i) distances[i] = -distances[i];
+    return;
+  }
   std::vector<float> ynorm(static_cast<size_t>(n));
   for (int64_t j = 0; j < n; ++j) ynorm[static_cast<size_t>(j)] = nrm2sq_seq(data + j * dim, dim);
   const int64_t k_eff = std::min(k, n);

@@ -48,7 +48,8 @@ void oracle_all_neighbors(const float* data, int64_t n, int64_t dim, int32_t met
                           int64_t* neighbors, float* distances, int32_t nthreads);
 
 /* mixer.cpp:843-864 brute_search_impl (blocked over queries; same per-element arithmetic).
-   nthreads > 1 splits queries across threads (results identical). */
+   nthreads > 1 splits queries across threads, or, for few queries against many rows, rows into
+   shards whose top-k lists merge in the reference's total order (results identical). */
 void oracle_brute_search(const float* data, int64_t n, int64_t dim, int32_t metric,
                          const float* queries, int64_t nq, int64_t k, const uint8_t* bitset,
                          int64_t* neighbors, float* distances, int32_t nthreads);

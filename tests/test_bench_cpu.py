@@ -71,3 +71,54 @@ def test_reference_sample_sizes_are_bounded():
     assert threads >= 1 and threads <= nq <= bench.CONFIGS["ivf"]["nq"]
     rows = bench._reference_kmeans_rows(bench.CONFIGS["c4"], 12.0)
     assert bench.CONFIGS["c4"]["clusters"] <= rows <= bench.CONFIGS["c4"]["n"]
+
+
+def _have_reference():
+    from oracle.cpu import REFERENCE_SO
+
+    return os.path.exists(REFERENCE_SO)
+
+
+def test_reference_sample_merge_equals_unsharded_search(monkeypatch):
+    """The bench's parity block merges the reference's per-shard answers; merged, they must be the
+    reference's answer over all rows (here: the restatement's unsharded search), for L2 and for
+    inner product (whose reported distances are negated scores), with duplicate rows across
+    shard boundaries and k above a shard's row count."""
+    import pytest
+
+    if not _have_reference():
+        pytest.skip("reference library not built")
+    from oracle.cpu import Oracle
+
+    monkeypatch.setattr(bench, "CHUNK", 700)
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal((2300, 16)).astype(np.float32)
+    x[1500] = x[20]  # equal distances on both sides of a shard boundary
+    x[699] = x[700]
+    q = rng.standard_normal((9, 16)).astype(np.float32)
+    q[3] = x[20]
+    for metric, k in (("l2", 10), ("inner_product", 7), ("l2", 650)):
+        cfg = dict(n=x.shape[0], k=k, metric=metric, dtype="f32")
+        _, nb, ds = bench._reference_sample(cfg, x, q, 3, q.shape[0])
+        rnb, rds = Oracle().brute_search(x, q, k, metric)
+        ke = min(k, x.shape[0])
+        assert np.array_equal(nb, rnb.reshape(-1, ke)), metric
+        assert np.array_equal(ds.view(np.uint32), rds.reshape(-1, ke).view(np.uint32)), metric
+        p = bench._parity(nb, ds, rnb.reshape(-1, ke), rds.reshape(-1, ke), 1e-4)
+        assert p["ok"] and p["id_mismatch"] == 0 and p["max_rel_err"] == 0.0
+
+
+def test_parity_flags_mismatches_beyond_ties():
+    nb_ref = np.array([[1, 2, 3]], np.int64)
+    ds_ref = np.array([[1.0, 2.0, 3.0]], np.float32)
+    # a near-tie swap at the last rank is allowed
+    p = bench._parity(np.array([[1, 2, 4]]), np.array([[1.0, 2.0, 3.0001]], np.float32),
+                      nb_ref, ds_ref, 1e-4)
+    assert p["ok"] and p["id_mismatch"] == 1 and p["id_mismatch_beyond_tie"] == 0
+    # a different neighbour with a clearly different distance is not
+    p = bench._parity(np.array([[1, 2, 4]]), np.array([[1.0, 2.0, 3.5]], np.float32),
+                      nb_ref, ds_ref, 1e-4)
+    assert not p["ok"] and p["id_mismatch_beyond_tie"] == 1
+    # same ids with different distance bits fail
+    p = bench._parity(nb_ref, np.array([[1.0, 2.0, 3.0000002]], np.float32), nb_ref, ds_ref, 1e-4)
+    assert not p["ok"] and p["distance_bits_differ_where_ids_agree"] == 1
