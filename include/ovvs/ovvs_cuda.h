@@ -78,9 +78,11 @@ OVVS_API ovvsStatus ovvsBruteForceSearchDevice(ovvsResources_t res, ovvsBruteFor
    (a framework's caching pool), or a latency-critical request loop where cudaMalloc/cudaFree and
    their implicit device synchronisation are not acceptable. This entry point has no counterpart
    in the reference. It allocates nothing: all intermediate buffers come from a fixed 32 MiB
-   device array built into the library (the runtime creates it once per device when the library's
-   module is loaded; it lives until the process exits). Its device address is looked up on the
-   first call on each device, so make that first call before any stream capture. Work runs on
+   device array built into the library, which lives until the process exits. The runtime creates
+   the array on a device when it loads that part of the library there; with CUDA's default lazy
+   module loading this is the first call on the device, which also looks up the array's address
+   (the one-time set-up). So make that first call at start-up, before another allocator takes the
+   device's free memory (or set CUDA_MODULE_LOADING=EAGER), and before any stream capture. Work runs on
    `stream` (NULL = the default stream) and the call returns after it has finished. Sizes whose
    buffers do not fit the array (about 4*dim + 16 + 8*list bytes per query, list = k plus a small
    margin rounded up to 4/8/16/32: some 50k queries of dim 128 at k = 10) are rejected with

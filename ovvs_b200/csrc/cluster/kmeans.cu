@@ -191,9 +191,10 @@ ovvsStatus fit(rt::Resources& r, const float* x, int64_t n_local, int64_t row_of
   OVVS_TRY_CUDA(m.d_centroids.reserve(cbytes));
   OVVS_TRY_CUDA(cudaMemcpyAsync(m.d_centroids.get(), init.data(), cbytes, cudaMemcpyHostToDevice, s));
   if (r.world > 1) {
-    OVVS_TRY(rt::status_of(ovvs::rt::nccl()->AllReduce(m.d_centroids.get(), m.d_centroids.get(),
-                                         static_cast<size_t>(k) * dim, ncclFloat32, ncclSum,
-                                         r.comm, s)));
+    OVVS_TRY(r.comm_ready());
+    OVVS_TRY(r.collective(ovvs::rt::nccl()->AllReduce(m.d_centroids.get(), m.d_centroids.get(),
+                                                      static_cast<size_t>(k) * dim, ncclFloat32,
+                                                      ncclSum, r.comm, s)));
   }
   const size_t xbytes = static_cast<size_t>(n_local) * dim * sizeof(float);
   OVVS_TRY_CUDA(m.d_x.reserve(xbytes + 16));
@@ -273,13 +274,17 @@ ovvsStatus fit(rt::Resources& r, const float* x, int64_t n_local, int64_t row_of
           m.d_x.as<float>(), static_cast<int>(dim), m.sorted_idx.as<uint32_t>(),
           m.counts.as<int>(), m.offsets.as<int>(), m.sum64.as<double>(), m.cnt64.as<double>());
       OVVS_TRY_CUDA(cudaGetLastError());
-      OVVS_TRY(rt::status_of(ovvs::rt::nccl()->GroupStart()));
-      OVVS_TRY(rt::status_of(ovvs::rt::nccl()->AllReduce(m.sum64.get(), m.sum64.get(),
-                                           static_cast<size_t>(k) * dim, ncclFloat64, ncclSum,
-                                           r.comm, s)));
-      OVVS_TRY(rt::status_of(ovvs::rt::nccl()->AllReduce(m.cnt64.get(), m.cnt64.get(), static_cast<size_t>(k),
-                                           ncclFloat64, ncclSum, r.comm, s)));
-      OVVS_TRY(rt::status_of(ovvs::rt::nccl()->GroupEnd()));
+      // Non-blocking communicator: the group's enqueue is settled (bounded) before the kernel
+      // that reads the sums is launched behind it.
+      const rt::NcclApi* nc = ovvs::rt::nccl();
+      OVVS_TRY(r.comm_ready());
+      OVVS_TRY(rt::status_of(nc->GroupStart()));
+      OVVS_TRY(r.collective(nc->AllReduce(m.sum64.get(), m.sum64.get(),
+                                          static_cast<size_t>(k) * dim, ncclFloat64, ncclSum,
+                                          r.comm, s)));
+      OVVS_TRY(r.collective(nc->AllReduce(m.cnt64.get(), m.cnt64.get(), static_cast<size_t>(k),
+                                          ncclFloat64, ncclSum, r.comm, s)));
+      OVVS_TRY(r.collective(nc->GroupEnd()));
       const int64_t total = static_cast<int64_t>(k) * dim;
       centroid_finish_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(
           m.sum64.as<double>(), m.cnt64.as<double>(), k, static_cast<int>(dim),

@@ -200,20 +200,6 @@ ovvsStatus build_from_host(rt::Resources& r, BruteIndex& ix, const void* data, i
   return r.finish();
 }
 
-namespace {
-
-// Per-search state shared by the small-k and large-k paths.
-struct SearchCtx {
-  int64_t q_pad = 0;
-  int num_qtiles = 0;
-  __half* a16 = nullptr;
-  float* q_mul = nullptr;
-  float* xn = nullptr;
-  int* flag = nullptr;
-  uint32_t* allow = nullptr;
-  prim::FusedMaps maps{};
-};
-
 // Fused-kernel parameters common to every launch of one search.
 ovvsStatus base_params(rt::Resources& r, const BruteIndex& ix, const SearchCtx& c, int64_t nq,
                        prim::FusedParams* out) {
@@ -264,10 +250,21 @@ prim::MergeParams merge_params(const BruteIndex& ix, const SearchCtx& c, const f
   return m;
 }
 
-// SMs the fused kernel can use at once: two per co-resident CTA pair.
 int pair_sms(const rt::Resources& r, const prim::FusedParams& p) {
   return 2 * std::min(r.num_sms / 2, prim::fused_max_pairs(p.smem_bytes));
 }
+
+ovvsStatus encode_query_maps(SearchCtx& c, int dp) {
+  const uint64_t a_cols = static_cast<uint64_t>(2 * dp);
+  if (!rt::encode_f16_2d(&c.maps.a64, c.a16, a_cols, c.q_pad, 64, kTileQ) ||
+      !rt::encode_f16_2d(&c.maps.a32, c.a16, a_cols, c.q_pad, 32, kTileQ) ||
+      !rt::encode_f16_2d(&c.maps.a16, c.a16, a_cols, c.q_pad, 16, kTileQ)) {
+    return OVVS_STATUS_ERROR;
+  }
+  return OVVS_STATUS_SUCCESS;
+}
+
+namespace {
 
 int launch_grid(const prim::FusedParams& p, int num_sms) {
   return prim::fused_grid(p.num_items, num_sms);
@@ -391,6 +388,37 @@ ovvsStatus prepare_queries(rt::Resources& r, const BruteIndex& ix, const float* 
   return OVVS_STATUS_SUCCESS;
 }
 
+ovvsStatus search_from_host(rt::Resources& r, const BruteIndex& ix, const float* queries,
+                            int64_t nq, int64_t k, const uint8_t* bitset, int64_t* neighbors,
+                            float* distances, int64_t* k_eff_out) {
+  const int64_t k_eff = std::min<int64_t>(k, ix.n_total);
+  float* dq = nullptr;
+  OVVS_TRY(r.scratch(rt::kWsQueries, static_cast<size_t>(nq) * ix.dim, &dq));
+  OVVS_TRY_CUDA(cudaMemcpyAsync(dq, queries, static_cast<size_t>(nq) * ix.dim * sizeof(float),
+                                cudaMemcpyHostToDevice, r.stream));
+  uint8_t* db = nullptr;
+  if (bitset) {
+    const int64_t bytes = (ix.row_offset + ix.n + 7) / 8;
+    OVVS_TRY(r.scratch(rt::kWsBitset, static_cast<size_t>(bytes), &db));
+    OVVS_TRY_CUDA(cudaMemcpyAsync(db, bitset, static_cast<size_t>(bytes), cudaMemcpyHostToDevice,
+                                  r.stream));
+  }
+  int64_t* dn = nullptr;
+  float* dd = nullptr;
+  OVVS_TRY(r.scratch(rt::kWsNeighbors, static_cast<size_t>(nq) * k_eff, &dn));
+  OVVS_TRY(r.scratch(rt::kWsDistances, static_cast<size_t>(nq) * k_eff, &dd));
+  int64_t ke = 0;
+  OVVS_TRY(search_device(r, ix, dq, nq, k, db, dn, dd, &ke));
+  if (neighbors) {
+    OVVS_TRY_CUDA(cudaMemcpyAsync(neighbors, dn, static_cast<size_t>(nq) * ke * sizeof(int64_t),
+                                  cudaMemcpyDeviceToHost, r.stream));
+    OVVS_TRY_CUDA(cudaMemcpyAsync(distances, dd, static_cast<size_t>(nq) * ke * sizeof(float),
+                                  cudaMemcpyDeviceToHost, r.stream));
+  }
+  *k_eff_out = ke;
+  return r.finish();
+}
+
 ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_queries, int64_t nq,
                          int64_t k, const uint8_t* d_bitset, int64_t* d_neighbors,
                          float* d_distances, int64_t* k_eff_out, const uint64_t* d_init_bound,
@@ -398,6 +426,7 @@ ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_
   cudaStream_t s = r.stream;
   const int64_t k_eff = std::min<int64_t>(k, ix.n_total);
   *k_eff_out = k_eff;
+  if (!ix.shards.empty()) return OVVS_STATUS_UNSUPPORTED;  // a group's index: its shards search
   if (ix.device != r.device) return OVVS_STATUS_INVALID_ARGUMENT;
   const int kl = list_size_for(k_eff);
   const int dim = static_cast<int>(ix.dim);
@@ -430,12 +459,7 @@ ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_
                             c.allow, s);
     OVVS_TRY_CUDA(cudaGetLastError());
   }
-  const uint64_t a_cols = static_cast<uint64_t>(2 * ix.dp);
-  if (!rt::encode_f16_2d(&c.maps.a64, c.a16, a_cols, c.q_pad, 64, kTileQ) ||
-      !rt::encode_f16_2d(&c.maps.a32, c.a16, a_cols, c.q_pad, 32, kTileQ) ||
-      !rt::encode_f16_2d(&c.maps.a16, c.a16, a_cols, c.q_pad, 16, kTileQ)) {
-    return OVVS_STATUS_ERROR;
-  }
+  OVVS_TRY(encode_query_maps(c, ix.dp));
   c.maps.b64 = ix.b64;
   c.maps.b32 = ix.b32;
   c.maps.b16 = ix.b16;
@@ -495,12 +519,15 @@ ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_
     r.mark(4);
     return OVVS_STATUS_SUCCESS;
   }
-  // Sharded: exact per-shard top-k, all-gather over NVLink, then an exact (rank, id) merge.
+  // Sharded: exact per-shard top-k, all-gather over NVLink, then an exact (rank, id) merge. The
+  // communicator is non-blocking: the group's enqueue is settled (bounded) before the merge kernel
+  // that reads the gathered lists is launched behind it.
   const rt::NcclApi* nc = rt::nccl();
+  OVVS_TRY(r.comm_ready());
   OVVS_TRY(rt::status_of(nc->GroupStart()));
-  OVVS_TRY(rt::status_of(nc->AllGather(srank, grank, cnt, ncclFloat32, r.comm, s)));
-  OVVS_TRY(rt::status_of(nc->AllGather(sgid, ggid, cnt, ncclInt64, r.comm, s)));
-  OVVS_TRY(rt::status_of(nc->GroupEnd()));
+  OVVS_TRY(r.collective(nc->AllGather(srank, grank, cnt, ncclFloat32, r.comm, s)));
+  OVVS_TRY(r.collective(nc->AllGather(sgid, ggid, cnt, ncclInt64, r.comm, s)));
+  OVVS_TRY(r.collective(nc->GroupEnd()));
   OVVS_TRY_CUDA(prim::launch_shard_merge(grank, ggid, r.world, nq, static_cast<int>(k_eff),
                                          m.negate_output, d_neighbors, d_distances, s));
   r.mark(4);

@@ -12,8 +12,13 @@
 #pragma once
 
 #include <cstdint>
+#include <memory>
+#include <vector>
+
+#include <cuda_fp16.h>
 
 #include "../prim/knn_fused.cuh"
+#include "../prim/select.cuh"
 #include "../rt/runtime.hpp"
 
 namespace ovvs {
@@ -39,6 +44,10 @@ struct BruteIndex {
   int chunk_w[prim::kMaxChunks] = {};
   rt::DeviceBuffer rows16, exact32, aux, tile_aux, norm_sorted, row_id, inv_perm;
   CUtensorMap b64{}, b32{}, b16{};
+  // Built by a Resources spanning several devices in one process: one shard per device (rank g
+  // holds rows [n*g/G, n*(g+1)/G)), and this object holds only the metadata above. A single entry
+  // means the dataset was too small to shard and lives on the group's first device.
+  std::vector<std::unique_ptr<BruteIndex>> shards;
 };
 
 // Builds (or rebuilds in place, reusing allocations) from rows already on the device.
@@ -73,6 +82,39 @@ ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_
                          float* d_distances, int64_t* k_eff_out,
                          const uint64_t* d_init_bound = nullptr,
                          const PreparedQueries* prepared = nullptr, bool labels_only = false);
+
+// A search of host queries through the device path on r: queries (and the bitset) copied in,
+// search_device, and, when `neighbors` is not null, the [nq x k_eff] results copied out; waits
+// for r's stream (finish). For a sharded index every rank calls it (the exchange is collective).
+ovvsStatus search_from_host(rt::Resources& r, const BruteIndex& ix, const float* queries,
+                            int64_t nq, int64_t k, const uint8_t* bitset, int64_t* neighbors,
+                            float* distances, int64_t* k_eff_out);
+
+// Per-search buffers and tensor maps shared by the fused kernel's launches of one search.
+struct SearchCtx {
+  int64_t q_pad = 0;
+  int num_qtiles = 0;
+  __half* a16 = nullptr;   // scaled fp16 query operand [q_pad x 2*dp]
+  float* q_mul = nullptr;  // per-query multiplier
+  float* xn = nullptr;     // per-query reference norm
+  int* flag = nullptr;     // query lo-part flag
+  uint32_t* allow = nullptr;
+  prim::FusedMaps maps{};
+};
+
+// Fused-kernel parameters common to every launch of one search.
+ovvsStatus base_params(rt::Resources& r, const BruteIndex& ix, const SearchCtx& c, int64_t nq,
+                       prim::FusedParams* out);
+
+// Merge + exact re-rank parameters of one search (outputs and candidate lists set by the caller).
+prim::MergeParams merge_params(const BruteIndex& ix, const SearchCtx& c, const float* d_queries,
+                               int64_t nq, int64_t k_eff);
+
+// SMs the fused kernel can use at once: two per co-resident CTA pair.
+int pair_sms(const rt::Resources& r, const prim::FusedParams& p);
+
+// Encodes c.maps' query tensor maps over c.a16.
+ovvsStatus encode_query_maps(SearchCtx& c, int dp);
 
 // Number of super-chunks per query tile for the fused kernel's work items (items = query tiles x
 // super-chunks), limited so the candidate lists stay under cand_per_sc_bytes * sc <= 1.5 GB.

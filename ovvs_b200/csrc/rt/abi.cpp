@@ -8,12 +8,15 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <memory>
 #include <new>
 #include <string>
+#include <vector>
 
 #include "../cluster/kmeans.hpp"
 #include "../neighbors/brute_force.hpp"
 #include "../prim/watchdog.cuh"
+#include "group.hpp"
 #include "ovvs/ovvs.h"
 #include "ovvs/ovvs_cuda.h"
 #include "runtime.hpp"
@@ -44,36 +47,21 @@ ovvs::km::KMeansModel* as_model(ovvsKMeansModel_t m) {
 
 bool mul_overflows(int64_t a, int64_t b, int64_t limit) { return a > 0 && b > limit / a; }
 
-// Host-buffer search through the device path, shared by ovvsBruteForceSearch and the batcher.
+// Host-buffer search through the device path (one device, or every device of a group).
 ovvsStatus search_host(Resources& r, ovvs::nb::BruteIndex& ix, const float* queries, int64_t nq,
                        int64_t k, const uint8_t* bitset, int64_t* neighbors, float* distances) {
   OVVS_TRY(r.check_policy());
   OVVS_TRY(r.activate());
   if (mul_overflows(nq, ix.dim, INT64_MAX / 8) || mul_overflows(nq, k, INT64_MAX / 8))
     return OVVS_STATUS_SHAPE_MISMATCH;
-  const int64_t k_eff = std::min<int64_t>(k, ix.n_total);
-  float* dq = nullptr;
-  OVVS_TRY(r.scratch(ovvs::rt::kWsQueries, static_cast<size_t>(nq) * ix.dim, &dq));
-  OVVS_TRY_CUDA(cudaMemcpyAsync(dq, queries, static_cast<size_t>(nq) * ix.dim * sizeof(float),
-                                cudaMemcpyHostToDevice, r.stream));
-  uint8_t* db = nullptr;
-  if (bitset) {
-    const int64_t bytes = (ix.row_offset + ix.n + 7) / 8;
-    OVVS_TRY(r.scratch(ovvs::rt::kWsBitset, static_cast<size_t>(bytes), &db));
-    OVVS_TRY_CUDA(cudaMemcpyAsync(db, bitset, static_cast<size_t>(bytes), cudaMemcpyHostToDevice,
-                                  r.stream));
-  }
-  int64_t* dn = nullptr;
-  float* dd = nullptr;
-  OVVS_TRY(r.scratch(ovvs::rt::kWsNeighbors, static_cast<size_t>(nq) * k_eff, &dn));
-  OVVS_TRY(r.scratch(ovvs::rt::kWsDistances, static_cast<size_t>(nq) * k_eff, &dd));
   int64_t ke = 0;
-  OVVS_TRY(ovvs::nb::search_device(r, ix, dq, nq, k, db, dn, dd, &ke));
-  OVVS_TRY_CUDA(cudaMemcpyAsync(neighbors, dn, static_cast<size_t>(nq) * ke * sizeof(int64_t),
-                                cudaMemcpyDeviceToHost, r.stream));
-  OVVS_TRY_CUDA(cudaMemcpyAsync(distances, dd, static_cast<size_t>(nq) * ke * sizeof(float),
-                                cudaMemcpyDeviceToHost, r.stream));
-  OVVS_TRY(r.finish());
+  if (!ix.shards.empty()) {
+    if (ix.shards.size() > 1 && r.group.size() != ix.shards.size())
+      return OVVS_STATUS_INVALID_ARGUMENT;  // searched through the group that built it
+    OVVS_TRY(ovvs::rt::group_search(r, ix, queries, nq, k, bitset, neighbors, distances, &ke));
+  } else {
+    OVVS_TRY(ovvs::nb::search_from_host(r, ix, queries, nq, k, bitset, neighbors, distances, &ke));
+  }
   // mixer.cpp:860-862: for INNER_PRODUCT the reference negates nq*k entries although only
   // nq*min(k,n) were written; entries past that are caller memory it flips in place.
   if (ix.metric == OVVS_METRIC_INNER_PRODUCT && k > ke) {
@@ -119,11 +107,26 @@ const char* ovvsStatusString(ovvsStatus status) {
 
 // ---- Resources (reference src/rt/resources.cpp:14-94) ------------------------------------
 
+// One device (OVVS_CUDA_DEVICE, else 0), or, when OVVS_CUDA_DEVICES names several, a group over
+// them: the hot path then shards over every listed device (group.hpp).
 ovvsStatus ovvsResourcesCreate(ovvsResources_t* res) {
   if (!res) return OVVS_STATUS_INVALID_ARGUMENT;
   auto* r = new (std::nothrow) Resources();
   if (!r) return OVVS_STATUS_OOM;
-  ovvs::rt::probe_device(*r, ovvs::rt::default_device());
+  const ovvsStatus st = guarded([&] {
+    const std::vector<int> devices = ovvs::rt::default_devices();
+    ovvs::rt::probe_device(*r, devices[0]);
+    r->nccl_timeout_ms = ovvs::rt::nccl_timeout_ms_default();
+    if (devices.size() > 1 && r->gpu_available) {
+      OVVS_TRY(r->activate());
+      OVVS_TRY(ovvs::rt::create_group(*r, devices));
+    }
+    return OVVS_STATUS_SUCCESS;
+  });
+  if (st != OVVS_STATUS_SUCCESS) {
+    delete r;
+    return st;
+  }
   *res = ovvs::rt::to_handle(r);
   return OVVS_STATUS_SUCCESS;
 }
@@ -310,7 +313,19 @@ ovvsStatus ovvsBruteForceBuildTyped(ovvsResources_t res, const void* dataset, in
                                     int64_t dim, ovvsMetric metric, ovvsDType dtype,
                                     ovvsBruteForceIndex_t* index) {
   if (!res || !dataset || !index || n <= 0 || dim <= 0) return OVVS_STATUS_INVALID_ARGUMENT;
-  return ovvsBruteForceBuildShard(res, dataset, n, dim, metric, dtype, 0, index);
+  Resources& r = *from_handle(res);
+  if (r.group.empty()) return ovvsBruteForceBuildShard(res, dataset, n, dim, metric, dtype, 0, index);
+  return guarded([&] {
+    std::lock_guard<std::mutex> lk(r.mu);
+    OVVS_TRY(r.check_policy());
+    OVVS_TRY(r.activate());
+    if (mul_overflows(n, dim, INT64_MAX / 8)) return OVVS_STATUS_SHAPE_MISMATCH;
+    auto ix = std::make_unique<ovvs::nb::BruteIndex>();
+    OVVS_TRY(ovvs::rt::group_build(r, *ix, dataset, static_cast<int>(dtype), n, dim,
+                                   static_cast<int>(metric)));
+    *index = reinterpret_cast<ovvsBruteForceIndex_t>(ix.release());
+    return OVVS_STATUS_SUCCESS;
+  });
 }
 
 ovvsStatus ovvsBruteForceSearch(ovvsResources_t res, ovvsBruteForceIndex_t index,
@@ -355,7 +370,25 @@ ovvsStatus ovvsKMeansFit(ovvsResources_t res, const float* dataset, int64_t n, i
                          int32_t nclusters, int32_t iters, ovvsKMeansModel_t* model) {
   if (!res || !dataset || !model || n <= 0 || dim <= 0 || nclusters <= 0)
     return OVVS_STATUS_INVALID_ARGUMENT;
-  return ovvsKMeansFitShard(res, dataset, n, 0, n, dim, nclusters, iters, model);
+  Resources& r = *from_handle(res);
+  if (r.group.empty()) return ovvsKMeansFitShard(res, dataset, n, 0, n, dim, nclusters, iters, model);
+  return guarded([&] {
+    std::lock_guard<std::mutex> lk(r.mu);
+    OVVS_TRY(r.check_policy());
+    OVVS_TRY(r.activate());
+    auto m = std::make_unique<ovvs::km::KMeansModel>();
+    m->k_reported = nclusters;
+    m->dim = dim;
+    m->device = r.device;
+    // cluster.cpp:54 runs max(4, iters) iterations; n > INT32_MAX leaves the model empty, as in
+    // the single-device path.
+    if (n <= INT32_MAX)
+      OVVS_TRY(ovvs::rt::group_kmeans_fit(r, dataset, n, dim, nclusters, std::max(4, iters), *m));
+    *model = reinterpret_cast<ovvsKMeansModel_t>(m.release());
+    r.last_device = OVVS_DEVICE_GPU;
+    r.last_compute_dtype = OVVS_DTYPE_F32;
+    return OVVS_STATUS_SUCCESS;
+  });
 }
 
 ovvsStatus ovvsKMeansPredict(ovvsResources_t res, ovvsKMeansModel_t model, const float* x,
@@ -534,12 +567,13 @@ ovvsStatus ovvsResourcesCreateSharded(ovvsResources_t* res, int32_t device, int3
   ovvs::rt::probe_device(*r, device);
   r->rank = rank;
   r->world = world;
+  r->nccl_timeout_ms = ovvs::rt::nccl_timeout_ms_default();
   ovvsStatus st = r->activate();
   if (st == OVVS_STATUS_SUCCESS && world > 1 && !ovvs::rt::nccl()) st = OVVS_STATUS_DEVICE_UNAVAILABLE;
   if (st == OVVS_STATUS_SUCCESS && world > 1) {
     ncclUniqueId u;
     std::memcpy(&u, nccl_id, sizeof(u));
-    st = ovvs::rt::status_of(ovvs::rt::nccl()->CommInitRank(&r->comm, world, u, rank));
+    st = guarded([&] { return ovvs::rt::init_comm(*r, u); });  // non-blocking, bounded
   }
   if (st != OVVS_STATUS_SUCCESS) {
     delete r;

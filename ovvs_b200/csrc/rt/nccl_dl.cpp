@@ -19,15 +19,19 @@ const NcclApi* nccl() {
     auto sym = [h](const char* name) { return dlsym(h, name); };
     api.GetUniqueId = reinterpret_cast<decltype(api.GetUniqueId)>(sym("ncclGetUniqueId"));
     api.CommInitRank = reinterpret_cast<decltype(api.CommInitRank)>(sym("ncclCommInitRank"));
+    api.CommInitRankConfig =
+        reinterpret_cast<decltype(api.CommInitRankConfig)>(sym("ncclCommInitRankConfig"));
     api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(sym("ncclCommDestroy"));
+    api.CommAbort = reinterpret_cast<decltype(api.CommAbort)>(sym("ncclCommAbort"));
     api.CommGetAsyncError =
         reinterpret_cast<decltype(api.CommGetAsyncError)>(sym("ncclCommGetAsyncError"));
     api.AllGather = reinterpret_cast<decltype(api.AllGather)>(sym("ncclAllGather"));
     api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(sym("ncclAllReduce"));
     api.GroupStart = reinterpret_cast<decltype(api.GroupStart)>(sym("ncclGroupStart"));
     api.GroupEnd = reinterpret_cast<decltype(api.GroupEnd)>(sym("ncclGroupEnd"));
-    if (api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.AllGather &&
-        api.AllReduce && api.GroupStart && api.GroupEnd)
+    if (api.GetUniqueId && api.CommInitRank && api.CommInitRankConfig && api.CommDestroy &&
+        api.CommAbort && api.CommGetAsyncError && api.AllGather && api.AllReduce &&
+        api.GroupStart && api.GroupEnd)
       ready = &api;
   });
   return ready;

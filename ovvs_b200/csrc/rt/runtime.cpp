@@ -5,8 +5,12 @@
 #include <chrono>
 #include <cstdlib>
 #include <cstring>
+#include <sstream>
 #include <thread>
 #include <vector>
+
+#include "group.hpp"
+#include "nccl_watch.hpp"
 
 namespace ovvs {
 namespace rt {
@@ -65,10 +69,64 @@ void DeviceBuffer::release() {
   bytes_ = 0;
 }
 
-int default_device() {
-  const char* s = std::getenv("OVVS_CUDA_DEVICE");
-  if (s && *s) return std::atoi(s);
-  return 0;
+std::vector<int> default_devices() {
+  std::vector<int> out;
+  const char* list = std::getenv("OVVS_CUDA_DEVICES");
+  if (list && *list) {
+    std::stringstream ss(list);
+    std::string item;
+    while (std::getline(ss, item, ','))
+      if (!item.empty()) out.push_back(std::atoi(item.c_str()));
+  }
+  if (out.empty()) {
+    const char* one = std::getenv("OVVS_CUDA_DEVICE");
+    out.push_back(one && *one ? std::atoi(one) : 0);
+  }
+  return out;
+}
+
+int64_t nccl_timeout_ms_default() {
+  const char* s = std::getenv("OVVS_NCCL_TIMEOUT_MS");
+  const long long v = s && *s ? std::atoll(s) : 0;
+  return v > 0 ? v : 60000;
+}
+
+namespace {
+
+int64_t now_ms() {
+  return std::chrono::duration_cast<std::chrono::milliseconds>(
+             std::chrono::steady_clock::now().time_since_epoch())
+      .count();
+}
+
+void short_pause() { std::this_thread::sleep_for(std::chrono::microseconds(50)); }
+
+}  // namespace
+
+ovvsStatus init_comm(Resources& r, const ncclUniqueId& id) {
+  const NcclApi* nc = nccl();
+  if (!nc) return OVVS_STATUS_DEVICE_UNAVAILABLE;
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  const ncclResult_t ret = nc->CommInitRankConfig(&r.comm, r.world, id, r.rank, &cfg);
+  return r.collective(ret);
+}
+
+void Resources::abort_comm() {
+  if (comm) nccl()->CommAbort(comm);
+  comm = nullptr;
+  comm_failed = true;
+}
+
+ovvsStatus Resources::collective(ncclResult_t ret) {
+  if (comm_failed) return OVVS_STATUS_ERROR;
+  const NcclApi* nc = nccl();
+  auto async_error = [&](ncclResult_t* st) {
+    return comm ? nc->CommGetAsyncError(comm, st) : ncclInvalidUsage;
+  };
+  const WatchResult w = settle_nccl(ret, async_error, now_ms, short_pause, nccl_timeout_ms);
+  if (w.abort) abort_comm();
+  return w.status;
 }
 
 void probe_device(Resources& r, int device) {
@@ -92,6 +150,16 @@ void probe_device(Resources& r, int device) {
 }
 
 Resources::~Resources() {
+  // Group members first, each from its own worker thread (their communicators are torn down
+  // together), then the workers.
+  if (workers) {
+    workers->run([&](int g) {
+      group[static_cast<size_t>(g)].reset();
+      return OVVS_STATUS_SUCCESS;
+    });
+    workers.reset();
+  }
+  group.clear();
   if (gpu_available) cudaSetDevice(device);
   for (auto& b : ws) b.release();
   if (comm) ovvs::rt::nccl()->CommDestroy(comm);
@@ -150,6 +218,32 @@ ovvsStatus Resources::activate() {
 }
 
 ovvsStatus Resources::finish() {
+  if (comm || comm_failed) {
+    auto stream_state = [&] {
+      const cudaError_t e = cudaStreamQuery(stream);
+      if (e == cudaSuccess) return StreamState::kIdle;
+      if (e == cudaErrorNotReady) return StreamState::kBusy;
+      return StreamState::kFailed;
+    };
+    auto async_error = [&](ncclResult_t* st) {
+      if (!comm) {
+        *st = ncclSuccess;  // already aborted: only the stream is left to drain
+        return ncclSuccess;
+      }
+      return nccl()->CommGetAsyncError(comm, st);
+    };
+    const WatchResult w = watch_stream(stream_state, async_error, now_ms, short_pause,
+                                       nccl_timeout_ms);
+    if (w.abort) {
+      abort_comm();
+      // the abort ends the collectives still waiting for a peer; what remains drains quickly
+      const WatchResult d = watch_stream(stream_state, async_error, now_ms, short_pause, 10000);
+      (void)d;
+      (void)cudaGetLastError();
+      return OVVS_STATUS_ERROR;
+    }
+    if (w.status != OVVS_STATUS_SUCCESS) return status_of(cudaStreamSynchronize(stream));
+  }
   OVVS_TRY_CUDA(cudaStreamSynchronize(stream));
   int err = 0;
   OVVS_TRY_CUDA(cudaMemcpy(&err, d_err, sizeof(int), cudaMemcpyDeviceToHost));
@@ -205,12 +299,13 @@ bool encode_f16_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t r
 
 ovvsStatus allreduce_i64_sum(Resources& r, int64_t* value) {
   if (r.world <= 1) return OVVS_STATUS_SUCCESS;
+  OVVS_TRY(r.comm_ready());
   int64_t* d = nullptr;
   OVVS_TRY(r.scratch<int64_t>(kWsFlags, 1, &d));
   OVVS_TRY_CUDA(cudaMemcpyAsync(d, value, sizeof(int64_t), cudaMemcpyHostToDevice, r.stream));
-  OVVS_TRY(status_of(ovvs::rt::nccl()->AllReduce(d, d, 1, ncclInt64, ncclSum, r.comm, r.stream)));
+  OVVS_TRY(r.collective(ovvs::rt::nccl()->AllReduce(d, d, 1, ncclInt64, ncclSum, r.comm, r.stream)));
   OVVS_TRY_CUDA(cudaMemcpyAsync(value, d, sizeof(int64_t), cudaMemcpyDeviceToHost, r.stream));
-  OVVS_TRY_CUDA(cudaStreamSynchronize(r.stream));
+  OVVS_TRY(r.finish());
   return OVVS_STATUS_SUCCESS;
 }
 

@@ -13,9 +13,11 @@
 
 #include <atomic>
 #include <cstdint>
+#include <memory>
 #include <mutex>
 #include <string>
 #include <utility>
+#include <vector>
 
 #include "nccl_dl.hpp"
 #include "ovvs/ovvs.h"
@@ -110,6 +112,8 @@ enum WorkSlot : int {
   kWsCount
 };
 
+class Workers;
+
 struct Resources {
   int device = 0;
   bool gpu_available = false;
@@ -123,7 +127,14 @@ struct Resources {
   cudaStream_t stream = nullptr;
   int rank = 0;
   int world = 1;
-  ncclComm_t comm = nullptr;
+  ncclComm_t comm = nullptr;       // non-blocking communicator of the world's ranks (world > 1)
+  bool comm_failed = false;        // aborted after an NCCL error or an expired deadline
+  int64_t nccl_timeout_ms = 60000; // deadline of NCCL set-up and of waits on collectives
+  // One process, several devices (ovvsResourcesCreate with OVVS_CUDA_DEVICES naming more than
+  // one): this object is an ordinary Resources on the first device, and `group` holds one member
+  // per device (rank g of world G, sharing a communicator) driven by one worker thread each.
+  std::vector<std::unique_ptr<Resources>> group;
+  std::unique_ptr<Workers> workers;
   int* d_err = nullptr;  // kernel watchdog word (device)
   int last_kernel_error = 0;  // last nonzero watchdog code seen by finish()
   static constexpr int kPhases = 4;
@@ -149,8 +160,17 @@ struct Resources {
   ovvsStatus activate();
   // FORCE_CPU / FORCE_NPU cannot be honoured: the forced device never falls back.
   ovvsStatus check_policy() const;
-  // Waits for the stream, then reads and clears the watchdog word.
+  // Waits for the stream, then reads and clears the watchdog word. With a communicator the wait
+  // polls the stream and the communicator's asynchronous error against nccl_timeout_ms; an NCCL
+  // error or the deadline aborts the communicator and returns ERROR.
   ovvsStatus finish();
+  // Return value of an NCCL call on `comm`: settles ncclInProgress (bounded); a failure aborts
+  // the communicator and gives ERROR. Calls after an abort give ERROR without touching NCCL.
+  ovvsStatus collective(ncclResult_t ret);
+  ovvsStatus comm_ready() const {
+    return comm && !comm_failed ? OVVS_STATUS_SUCCESS : OVVS_STATUS_ERROR;
+  }
+  void abort_comm();
   // Records phase boundary `i` (0..kPhases) of the current search when profiling (ignored while
   // mark_hold is set: a k-means fit keeps its own phases while its searches run).
   void mark(int i);
@@ -184,8 +204,16 @@ ovvsStatus upload(Resources& r, void* dst, const void* src, size_t bytes);
 // Global row count of a sharded dataset (sum over ranks) and other small all-reduces.
 ovvsStatus allreduce_i64_sum(Resources& r, int64_t* value);
 
-// Default CUDA device for ovvsResourcesCreate: OVVS_CUDA_DEVICE, else 0.
-int default_device();
+// Devices for ovvsResourcesCreate: OVVS_CUDA_DEVICES (comma-separated, e.g. "0,1,2,3"), else
+// OVVS_CUDA_DEVICE, else 0.
+std::vector<int> default_devices();
+
+// Creates r's communicator as rank r.rank of r.world from `id` (non-blocking, bounded by
+// r.nccl_timeout_ms). r's device must be current.
+ovvsStatus init_comm(Resources& r, const ncclUniqueId& id);
+
+// Deadline for NCCL set-up and waits: OVVS_NCCL_TIMEOUT_MS, else 60 s.
+int64_t nccl_timeout_ms_default();
 
 }  // namespace rt
 }  // namespace ovvs

@@ -11,6 +11,8 @@ after every other test has run; it also passes alone in a fresh process.
 import numpy as np
 import pytest
 
+from tests.helpers import assert_search_close
+
 pytestmark = pytest.mark.gpu
 
 
@@ -23,7 +25,7 @@ def _device_arrays(torch, q, nq, k):
 
 @pytest.mark.parametrize("metric,dtype", [("l2", "f16"), ("inner_product", "f32"),
                                           ("cosine", "f32")])
-def test_no_alloc_matches_regular_search_twice(metric, dtype, ovvs, gpu):
+def test_no_alloc_matches_regular_search_twice(metric, dtype, ovvs, gpu, oracle):
     import torch
 
     rng = np.random.default_rng(2024)
@@ -38,15 +40,31 @@ def test_no_alloc_matches_regular_search_twice(metric, dtype, ovvs, gpu):
     ix.search_device(dq, k, ref_n, ref_d)
     gpu.synchronize()
     stream = torch.cuda.current_stream().cuda_stream
-    for call in range(2):  # the scratch array keeps the previous call's contents
-        _, got_n, got_d = _device_arrays(torch, q, 1000, k)
-        torch.cuda.synchronize()
+    outs = [_device_arrays(torch, q, 1000, k)[1:] for _ in range(2)]
+    torch.cuda.synchronize()
+    free = []
+    for call, (got_n, got_d) in enumerate(outs):  # the array keeps the previous call's contents
         ix.search_device_no_alloc(dq, k, got_n, got_d, stream=stream)
+        free.append(torch.cuda.mem_get_info()[0])
         assert torch.equal(got_n, ref_n), f"ids differ on call {call}"
         # same kernels and inputs: the distances are bit-identical, within any tolerance
         assert np.array_equal(got_d.cpu().numpy().view(np.uint32),
                               ref_d.cpu().numpy().view(np.uint32)), f"distances on call {call}"
+    # the first call on the device may load the array; later calls take no device memory at all
+    assert free[1] == free[0], f"free device memory changed by {free[0] - free[1]} bytes"
     ix.close()
+    # and the results are the reference's (the CPU oracle: ids equal, distances bit-identical
+    # but for near-ties at the k-th distance within the parity tolerance)
+    data32 = data.astype(np.float32)
+    rnb, rds = oracle.brute_search(data32, q, k, metric)
+
+    def exact(qi, rid):
+        v = oracle.pairwise(metric, q[qi:qi + 1], data32[rid:rid + 1])[0, 0]
+        return -v if metric == "inner_product" else v
+
+    assert_search_close(outs[1][0].cpu().numpy(), outs[1][1].cpu().numpy(), rnb, rds, k, exact,
+                        2e-3 if dtype == "f16" else 1e-4, what=f"no-alloc {metric}/{dtype}",
+                        atol_floor=1.0)
 
 
 def test_no_alloc_with_bitset_and_rejects_oversize(ovvs, gpu):
