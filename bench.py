@@ -395,16 +395,20 @@ def _reference_sizes(cfg, seconds):
     return threads, nq
 
 
-def _reference_kmeans_sample(cfg, data_host, rows):
+def _reference_kmeans_sample(cfg, data_host, rows, out=None):
     """Times the reference's FORCE_CPU ovvsKMeansFit (its minimum of 4 iterations) on the first
-    `rows` rows with the config's cluster count. Returns (seconds, iterations)."""
+    `rows` rows with the config's cluster count. Returns (seconds, iterations); the fitted
+    centroids go to out["centroids"] when `out` is given (the fit is timed, the copy is not)."""
     from oracle.cpu import Reference
 
     ref = Reference()
     x = np.ascontiguousarray(data_host[:rows], np.float32)
     t0 = time.perf_counter()
-    ref.kmeans(x, cfg["clusters"], 4, predict=False)
-    return time.perf_counter() - t0, 4
+    cents = ref.kmeans(x, cfg["clusters"], 4, predict=False)[0]
+    secs = time.perf_counter() - t0
+    if out is not None:
+        out["centroids"] = cents
+    return secs, 4
 
 
 def _reference_kmeans_rows(cfg, seconds):
@@ -794,12 +798,34 @@ def run_kmeans(args, cfg):
         dist.destroy_process_group()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rows = _reference_kmeans_rows(cfg, args.ref_seconds)
-        secs, it = _reference_kmeans_sample(cfg, shard_host, rows)
+        ref_out = {}
+        secs, it = _reference_kmeans_sample(cfg, shard_host, rows, ref_out)
         value, sample = _reference_kmeans_line(args, cfg, [secs], rows, it)
         line["cpu_baseline"] = {"value": value, "unit": "iterations/s", "cores": 1,
                                 "kind": "reference", "sample": sample}
+        # The same fit on this library (same rows, clusters and iterations; both seed with the
+        # reference's mt19937(42) row sample): centroids must be bit-identical.
+        res = ov.Resources.sharded(local, 0, 1, None)
+        m = ov.KMeans(np.ascontiguousarray(shard_host[:rows]), nclusters=C, iters=it,
+                      resources=res)
+        ours = m.centroids()
+        m.close()
+        res.close()
+        ref_c = ref_out["centroids"]
+        same = (ours.shape == ref_c.shape and
+                np.array_equal(ours.view(np.uint32), ref_c.view(np.uint32)))
+        rel = float(np.max(np.abs(ours.astype(np.float64) - ref_c) /
+                           np.maximum(np.abs(ref_c.astype(np.float64)), 1e-30))) \
+            if ours.shape == ref_c.shape else float("inf")
+        line["parity"] = {"rows": rows, "clusters": C, "iters": it,
+                          "centroids_bit_identical": bool(same), "max_rel_err": rel,
+                          "ok": bool(same),
+                          "against": "the reference library (oracle/_ref), FORCE_CPU, same rows"}
     if rank == 0:
         print(json.dumps(line), flush=True)
+        if "parity" in line and not line["parity"]["ok"]:
+            print("parity FAILED against the reference", file=sys.stderr)
+            return 1
     return 0
 
 

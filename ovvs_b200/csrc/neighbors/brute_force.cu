@@ -57,7 +57,7 @@ bool plan_chunks(int dp, int cap, int* nchunk, int* cx, int* cw) {
 
 int list_size_for(int64_t k_eff) {
   const int64_t need = k_eff + std::max<int64_t>(2, (k_eff + 7) / 8);
-  for (int kl : {4, 8, 16, 32})
+  for (int kl : {4, 8, 12, 16, 32})
     if (need <= kl) return kl;
   return 0;
 }

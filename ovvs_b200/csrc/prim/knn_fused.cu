@@ -575,11 +575,15 @@ __device__ __forceinline__ float append_limit(float tau, float2 ta) {
 }
 
 template <int KL>
-__device__ __forceinline__ void read_bound(const FusedParams& p, int64_t q, EpiState<KL>& st) {
-  const uint64_t b = __ldcg(reinterpret_cast<const unsigned long long*>(p.q_bound + q));
+__device__ __forceinline__ void apply_bound(uint64_t b, EpiState<KL>& st) {
   const float w = keys::key_value(b);
   const float mag = fabsf(w) + fabsf(st.ta.x) + fabsf(st.ta.y);
   st.gw = w + mag * 1e-5f;
+}
+
+template <int KL>
+__device__ __forceinline__ void read_bound(const FusedParams& p, int64_t q, EpiState<KL>& st) {
+  apply_bound<KL>(__ldcg(reinterpret_cast<const unsigned long long*>(p.q_bound + q)), st);
 }
 
 template <int KL>
@@ -731,6 +735,7 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
     // changes, when the shared bound is re-read, or after an insertion, not on every tile. The
     // next group's range is loaded one tile before it is needed.
     int g_cur = (it.t0 * p.tile_stride) >> kGroupShift, g_pf = -1;
+    uint64_t bound_pf = kEmptyKey;
     float2 ta_pf = make_float2(0.f, 0.f);
     st.ta = p.group_aux[g_cur];
     if constexpr (KL > 0) {
@@ -759,9 +764,13 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
         }
       }
       if constexpr (KL > 0) {
-        if (((t - it.t0) & (kBoundPeriod - 1)) == kBoundPeriod - 1 && st.real) {
+        // The shared bound is read a tile before it is used, so the load's latency is hidden.
+        const int phase_t = (t - it.t0) & (kBoundPeriod - 1);
+        if (phase_t == kBoundPeriod - 2 && st.real)
+          bound_pf = __ldcg(reinterpret_cast<const unsigned long long*>(p.q_bound + q));
+        if (phase_t == kBoundPeriod - 1 && st.real) {
           publish_bound<KL>(p, q, st);
-          read_bound<KL>(p, q, st);
+          apply_bound<KL>(bound_pf, st);
           refresh = true;
         }
       } else if (refresh) {
@@ -1028,6 +1037,8 @@ cudaError_t launch_knn_fused(const FusedMaps& maps, const FusedParams& p, int kl
       return launch_kl<4>(maps, p, grid, stream);
     case 8:
       return launch_kl<8>(maps, p, grid, stream);
+    case 12:
+      return launch_kl<12>(maps, p, grid, stream);
     case 16:
       return launch_kl<16>(maps, p, grid, stream);
     case 32:

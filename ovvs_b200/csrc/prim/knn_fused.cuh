@@ -163,7 +163,7 @@ inline int fused_grid(int num_items, int num_sms) {
   return 2 * (pairs > 0 ? pairs : 1);
 }
 
-// Host-side launcher (knn_fused.cu). `kl` in {4, 8, 16, 32} (sorted register lists), or 0 for
+// Host-side launcher (knn_fused.cu). `kl` in {4, 8, 12, 16, 32} (sorted register lists), or 0 for
 // append mode. `grid` is even (clusters of 2).
 cudaError_t launch_knn_fused(const FusedMaps& maps, const FusedParams& p, int kl, int grid,
                              cudaStream_t stream);

@@ -443,6 +443,8 @@ cudaError_t launch_merge_rerank(const MergeParams& p, cudaStream_t stream) {
       return launch_kl<4>(p, stream);
     case 8:
       return launch_kl<8>(p, stream);
+    case 12:
+      return launch_kl<12>(p, stream);
     case 16:
       return launch_kl<16>(p, stream);
     case 32:

@@ -132,7 +132,7 @@ def test_ragged_sizes(n, nq, k, ovvs, gpu, oracle):
     _run_parity(ovvs, gpu, oracle, "l2", "f32", n=n, dim=12, nq=nq, k=k, seed=n)
 
 
-@pytest.mark.parametrize("k", [1, 2, 4, 10, 16, 28])
+@pytest.mark.parametrize("k", [1, 2, 4, 8, 10, 11, 16, 28])
 def test_list_sizes(k, ovvs, gpu, oracle):
     _run_parity(ovvs, gpu, oracle, "inner_product", "f16", n=20000, dim=64, nq=200, k=k, seed=k,
                 kind="unit", fp16_queries=True)
