@@ -2,7 +2,9 @@
 #include "runtime.hpp"
 
 #include <algorithm>
+#include <atomic>
 #include <chrono>
+#include <memory>
 #include <cstdlib>
 #include <cstring>
 #include <sstream>
@@ -113,9 +115,21 @@ ovvsStatus init_comm(Resources& r, const ncclUniqueId& id) {
 }
 
 void Resources::abort_comm() {
-  if (comm) nccl()->CommAbort(comm);
+  ncclComm_t c = comm;
   comm = nullptr;
   comm_failed = true;
+  if (!c) return;
+  // ncclCommAbort ends the communicator's kernels still waiting for a peer, but its teardown can
+  // itself wait on a peer that is gone. It runs on a helper thread; the caller waits a bounded
+  // time and returns its error either way.
+  auto done = std::make_shared<std::atomic<bool>>(false);
+  std::thread([c, done] {
+    nccl()->CommAbort(c);
+    done->store(true);
+  }).detach();
+  const int64_t t0 = now_ms();
+  while (!done->load() && now_ms() - t0 < 5000) short_pause();
+  if (!done->load()) abort_pending = true;
 }
 
 ovvsStatus Resources::collective(ncclResult_t ret) {
@@ -160,6 +174,12 @@ Resources::~Resources() {
     workers.reset();
   }
   group.clear();
+  if (abort_pending) {
+    // A collective of the aborted communicator may still run: freeing could wait on it.
+    for (auto& b : ws) b.abandon();
+    d_err = nullptr;
+    stage_buf[0] = stage_buf[1] = nullptr;
+  }
   if (gpu_available) cudaSetDevice(device);
   for (auto& b : ws) b.release();
   if (comm) ovvs::rt::nccl()->CommDestroy(comm);
@@ -237,8 +257,10 @@ ovvsStatus Resources::finish() {
     if (w.abort) {
       abort_comm();
       // the abort ends the collectives still waiting for a peer; what remains drains quickly
-      const WatchResult d = watch_stream(stream_state, async_error, now_ms, short_pause, 10000);
-      (void)d;
+      if (!abort_pending) {
+        const WatchResult d = watch_stream(stream_state, async_error, now_ms, short_pause, 10000);
+        (void)d;
+      }
       (void)cudaGetLastError();
       return OVVS_STATUS_ERROR;
     }

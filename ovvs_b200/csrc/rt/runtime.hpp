@@ -58,6 +58,12 @@ class DeviceBuffer {
     std::swap(bytes_, o.bytes_);
     std::swap(device_, o.device_);
   }
+  // Forgets the allocation without freeing it (it is returned when the process exits). Used when
+  // freeing could wait on device work that may never finish (a collective whose peer is gone).
+  void abandon() noexcept {
+    ptr_ = nullptr;
+    bytes_ = 0;
+  }
   void* get() const { return ptr_; }
   size_t size() const { return bytes_; }
   template <class T>
@@ -129,6 +135,9 @@ struct Resources {
   int world = 1;
   ncclComm_t comm = nullptr;       // non-blocking communicator of the world's ranks (world > 1)
   bool comm_failed = false;        // aborted after an NCCL error or an expired deadline
+  // The abort did not finish within its bound (it waits on a departed peer): collectives may still
+  // occupy the device, so this Resources leaves its device memory to the process's exit.
+  bool abort_pending = false;
   int64_t nccl_timeout_ms = 60000; // deadline of NCCL set-up and of waits on collectives
   // One process, several devices (ovvsResourcesCreate with OVVS_CUDA_DEVICES naming more than
   // one): this object is an ordinary Resources on the first device, and `group` holds one member

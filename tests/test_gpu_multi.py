@@ -149,9 +149,16 @@ def test_plain_abi_over_two_gpus(ovvs, gpu, oracle):
     assert np.mean(labels == ref_labels) > 0.999
 
 
-def _leaving_worker(rank, uid, out, go):
-    """Rank 1 leaves after the first search (nothing in flight); rank 0 then searches again."""
+def _leaving_worker(rank, uid, out, go, log_path):
+    """Rank 1 leaves after the first search (nothing in flight); rank 0 then searches again. Each
+    step of rank 0 is logged (flushed) so that a stall shows where it happened."""
     import time
+
+    def log(msg):
+        with open(log_path, "a") as f:
+            f.write(f"{time.time():.3f} rank {rank}: {msg}\n")
+            f.flush()
+            os.fsync(f.fileno())
 
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     os.environ["OVVS_NCCL_TIMEOUT_MS"] = "10000"
@@ -174,6 +181,7 @@ def _leaving_worker(rank, uid, out, go):
         if rank == 1:
             leave((1, "left", None))  # leaves between steps: its search has completed
         go.wait(timeout=120)  # rank 1 has exited
+        log("peer gone; searching")
         t0 = time.perf_counter()
         try:
             ix.search(queries, K)
@@ -181,17 +189,19 @@ def _leaving_worker(rank, uid, out, go):
         except ov.OvvsError as e:
             status = e.status
         took = time.perf_counter() - t0
+        log(f"search returned status {status} after {took:.1f} s")
         try:
             ix.search(queries, K)  # the communicator is gone: fails at once
             again = 0
         except ov.OvvsError as e:
             again = e.status
+        log(f"second search returned status {again}")
         leave((0, (status, took, again, time.perf_counter() - t0 - took), None))
     except Exception as e:
         out.put((rank, None, repr(e)))
 
 
-def test_rank_leaving_between_steps_fails_closed(ovvs, gpu):
+def test_rank_leaving_between_steps_fails_closed(ovvs, gpu, tmp_path):
     """One of two ranks exits between searches; the other's next search ends with
     OVVS_STATUS_ERROR once the NCCL deadline (10 s here) passes, the communicator is aborted, and
     later searches fail immediately instead of hanging (fail closed, src/prim/mixer.cpp:47-50)."""
@@ -203,7 +213,9 @@ def test_rank_leaving_between_steps_fails_closed(ovvs, gpu):
     out = ctx.Queue()
     go = ctx.Event()
     uid = ovvs.nccl_unique_id()
-    procs = [ctx.Process(target=_leaving_worker, args=(r, uid, out, go)) for r in range(2)]
+    log_path = str(tmp_path / "ranks.log")
+    procs = [ctx.Process(target=_leaving_worker, args=(r, uid, out, go, log_path))
+             for r in range(2)]
     for p in procs:
         p.start()
     try:
@@ -211,7 +223,11 @@ def test_rank_leaving_between_steps_fails_closed(ovvs, gpu):
         assert err is None and rank == 1 and msg == "left", (rank, msg, err)
         procs[1].join(timeout=60)
         go.set()
-        rank, res, err = out.get(timeout=120)
+        try:
+            rank, res, err = out.get(timeout=90)
+        except Exception:
+            log = open(log_path).read() if os.path.exists(log_path) else "(no log)"
+            raise AssertionError("rank 0 did not report after its peer left:\n" + log)
         assert err is None, err
         status, took, again, took_again = res
         assert status == 1, f"search after a rank left returned {status}"  # OVVS_STATUS_ERROR

@@ -141,3 +141,23 @@ def test_ivf_flat_probing_every_list_is_brute_force(oracle):
         bnb, bds = oracle.brute_search(x, q, 9, metric)
         assert np.all(same_bits(ds.ravel(), bds)), metric
         assert np.mean(nb.ravel() == bnb) > 0.99, metric
+
+
+def test_row_sharded_oracle_equals_serial(oracle):
+    """Few queries over many rows take the oracle's row-sharded path (each thread a row shard,
+    shard lists merged in the reference's total order): it must equal the serial search bit for
+    bit, with NaN rows, duplicate rows across shard boundaries, bitsets and every metric."""
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((70_000, 24)).astype(np.float32)
+    x[36_000] = x[5]
+    x[200] = np.nan
+    q = rng.standard_normal((5, 24)).astype(np.float32)
+    q[1] = x[5]
+    bits = np.packbits((rng.random(70_000) < 0.7).astype(np.uint8), bitorder="little")
+    for metric in ("l2", "inner_product", "cosine", "hamming", "lp", "l2_sqrt"):
+        for k in (1, 10, 100):
+            for b in (None, bits):
+                a = oracle.brute_search(x, q, k, metric, bitset=b, nthreads=1)
+                c = oracle.brute_search(x, q, k, metric, bitset=b, nthreads=16)
+                assert np.array_equal(a[0], c[0]), (metric, k)
+                assert np.array_equal(a[1].view(np.uint32), c[1].view(np.uint32)), (metric, k)
