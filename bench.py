@@ -45,6 +45,11 @@ CONFIGS = {
     "c3s": dict(metric="l2", dtype="f16", n=2_000_000, dim=128, nq=10_000, k=10, dist="mixture",
                 centres=1024, centre_std=2.0, seed=2,
                 desc="L2 fp16, N=2M x 128 Gaussian mixture (1024 centres), Q=10k, k=10"),
+    # one rank's share of config 3 on 8 GPUs (1.25M rows), searched by one GPU: the per-rank kernel
+    "c3r": dict(metric="l2", dtype="f16", n=1_250_000, dim=128, nq=10_000, k=10, dist="mixture",
+                centres=1024, centre_std=2.0, seed=2,
+                desc="L2 fp16, N=1.25M x 128 Gaussian mixture (1024 centres), Q=10k, k=10 "
+                     "(one rank's rows of config 3 on 8 GPUs)"),
     # small query batch over config 3's database: one pair tile of 256 queries, HBM-bound
     "c3b": dict(metric="l2", dtype="f16", n=10_000_000, dim=128, nq=256, k=10, dist="mixture",
                 centres=1024, centre_std=2.0, seed=2, bound="hbm",
@@ -616,11 +621,13 @@ def run_ours(args, cfg):
                 "kernel": "knn_fused_kernel", "bytes_per_launch": hbm_bytes,
                 "peak_source": f"{peak_kind} HBM copy bandwidth"}
     else:
+        # One fused launch per search (~25 ms on config 3), timed in a region well under a second:
+        # the burst figure is the kernel's ceiling (the sustained one is for seconds-long steps).
         roof = {"bound": "tensor", "achieved": flops / (fused_ms / 1e3) / 1e12,
-                "peak": float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))),
+                "peak": float(peaks.get("bf16_tflops", peaks.get("bf16_tflops_sustained"))),
                 "unit": "TFLOP/s", "traffic": traffic, "kernel": "knn_fused_kernel",
                 "flops_per_launch": flops,
-                "peak_source": f"{peak_kind} bf16 dense sustained (fp16 MMA rate)"}
+                "peak_source": f"{peak_kind} bf16 dense burst (fp16 MMA rate)"}
     roof["frac"] = roof["achieved"] / roof["peak"]
     clk = clocks.summary()
 

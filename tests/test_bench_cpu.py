@@ -46,8 +46,9 @@ def test_metric_names():
 
 
 def test_traffic_figures_come_from_the_committed_profile():
-    assert bench._traffic_from_profiles("c3s") == 821530624.0
-    assert bench._traffic_from_profiles("c3") == 5 * 821530624.0
+    # both measured (read + write bytes of one launch), not scaled from a smaller case
+    assert bench._traffic_from_profiles("c3s") == 793717504.0 + 22001408.0
+    assert bench._traffic_from_profiles("c3") == 16770861824.0 + 50106624.0
     assert bench._traffic_from_profiles("no-such-config") is None
 
 
