@@ -170,6 +170,7 @@ std::vector<int64_t> init_rows(int64_t n, int32_t k) {
 ovvsStatus fit(rt::Resources& r, const float* x, int64_t n_local, int64_t row_offset,
                int64_t n_total, int64_t dim, int32_t nclusters, int32_t iters, KMeansModel& m) {
   cudaStream_t s = r.stream;
+  if (r.world > 1) OVVS_TRY(r.comm_ready());  // after a communicator failure: fail at once
   m.device = r.device;
   m.k_reported = nclusters;
   m.dim = dim;
@@ -199,7 +200,7 @@ ovvsStatus fit(rt::Resources& r, const float* x, int64_t n_local, int64_t row_of
   const size_t xbytes = static_cast<size_t>(n_local) * dim * sizeof(float);
   OVVS_TRY_CUDA(m.d_x.reserve(xbytes + 16));
   OVVS_TRY(rt::upload(r, m.d_x.get(), x, xbytes));
-  OVVS_TRY_CUDA(cudaStreamSynchronize(s));  // `init` is a host temporary
+  OVVS_TRY(r.finish());  // `init` is a host temporary (bounded wait: the seeding all-reduce)
 
   const int64_t n = n_local;
   OVVS_TRY_CUDA(m.labels.reserve(n * sizeof(int64_t) + 16));
@@ -293,6 +294,9 @@ ovvsStatus fit(rt::Resources& r, const float* x, int64_t n_local, int64_t row_of
     }
   }
   r.mark_hold = false;
+  // Sharded: the last iteration's all-reduce is waited for with a bound before anything below
+  // (frees, copies into pageable host memory) could wait on it without one.
+  if (r.world > 1) OVVS_TRY(r.finish());
   r.mark(2);
   // free the per-fit query operands
   m.prepared.a16.release();

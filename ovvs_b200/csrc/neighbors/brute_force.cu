@@ -409,6 +409,10 @@ ovvsStatus search_from_host(rt::Resources& r, const BruteIndex& ix, const float*
   OVVS_TRY(r.scratch(rt::kWsDistances, static_cast<size_t>(nq) * k_eff, &dd));
   int64_t ke = 0;
   OVVS_TRY(search_device(r, ix, dq, nq, k, db, dn, dd, &ke));
+  // A copy into pageable host memory returns only once the stream's earlier work is done, so with
+  // the exchange of a sharded search in the stream it would wait without a bound on the peers:
+  // the bounded wait comes first.
+  if (ix.sharded) OVVS_TRY(r.finish());
   if (neighbors) {
     OVVS_TRY_CUDA(cudaMemcpyAsync(neighbors, dn, static_cast<size_t>(nq) * ke * sizeof(int64_t),
                                   cudaMemcpyDeviceToHost, r.stream));
@@ -428,6 +432,8 @@ ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_
   *k_eff_out = k_eff;
   if (!ix.shards.empty()) return OVVS_STATUS_UNSUPPORTED;  // a group's index: its shards search
   if (ix.device != r.device) return OVVS_STATUS_INVALID_ARGUMENT;
+  // Sharded after a communicator failure: fail before touching the stream or the workspaces.
+  if (ix.sharded) OVVS_TRY(r.comm_ready());
   const int kl = list_size_for(k_eff);
   const int dim = static_cast<int>(ix.dim);
 

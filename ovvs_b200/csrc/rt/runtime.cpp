@@ -326,8 +326,8 @@ ovvsStatus allreduce_i64_sum(Resources& r, int64_t* value) {
   OVVS_TRY(r.scratch<int64_t>(kWsFlags, 1, &d));
   OVVS_TRY_CUDA(cudaMemcpyAsync(d, value, sizeof(int64_t), cudaMemcpyHostToDevice, r.stream));
   OVVS_TRY(r.collective(ovvs::rt::nccl()->AllReduce(d, d, 1, ncclInt64, ncclSum, r.comm, r.stream)));
-  OVVS_TRY_CUDA(cudaMemcpyAsync(value, d, sizeof(int64_t), cudaMemcpyDeviceToHost, r.stream));
-  OVVS_TRY(r.finish());
+  OVVS_TRY(r.finish());  // bounded wait before the (blocking) copy into host memory
+  OVVS_TRY_CUDA(cudaMemcpy(value, d, sizeof(int64_t), cudaMemcpyDeviceToHost));
   return OVVS_STATUS_SUCCESS;
 }
 
