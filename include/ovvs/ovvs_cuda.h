@@ -82,10 +82,10 @@ OVVS_API ovvsStatus ovvsBruteForceSearchDevice(ovvsResources_t res, ovvsBruteFor
    the array on a device when it loads that part of the library there; with CUDA's default lazy
    module loading this is the first call on the device, which also looks up the array's address
    (the one-time set-up). So make that first call at start-up, before another allocator takes the
-   device's free memory (or set CUDA_MODULE_LOADING=EAGER), and before any stream capture. Work runs on
+   device's free memory (or set CUDA_MODULE_LOADING=EAGER). Work runs on
    `stream` (NULL = the default stream) and the call returns after it has finished. Sizes whose
    buffers do not fit the array (about 4*dim + 16 + 8*list bytes per query, list = k plus a small
-   margin rounded up to 4/8/16/32: some 50k queries of dim 128 at k = 10) are rejected with
+   margin rounded up to 4/8/12/16/32: some 50k queries of dim 128 at k = 10) are rejected with
    OVVS_STATUS_SHAPE_MISMATCH;
    sharded indexes and k above the register-list limit return OVVS_STATUS_UNSUPPORTED. All calls on
    a device share the array and keep the last call's contents; the library clears what must start

@@ -548,12 +548,17 @@ struct EpiState {
   int64_t qi;     // this lane's query index
   uint64_t gkey;  // append mode: the query's bound key
   bool by_key;    // append mode: compare keys (bound value not finite, or exact mode)
+  int kpub;       // 4-entry lists: index of the entry that bounds the query (k_pub - 1), or -1
 };
 
 // Ranking value the filter compares against: the list's own worst entry, tightened by the
-// shared per-query bound. The bound gets a relative slack of 1e-5 of the magnitudes involved so
-// that rows tied with it within the ranking values' rounding still pass (the exact re-rank then
-// orders them).
+// shared per-query bound and, for 4-entry lists (k <= 2: k-means and coarse assignment, k = 1),
+// by the list's own k_pub-th entry. Both bounds get a relative slack of 1e-5 of the magnitudes
+// involved so that rows tied with them within the ranking values' rounding still pass (the exact
+// re-rank then orders them). The own k_pub-th entry is the bound this list publishes every
+// kBoundPeriod tiles; applying it at once matters where the list is much longer than k and items
+// are short (a k-means item spans all centroids in a few tiles). With longer lists the extra
+// selection on every refresh cost more than it saved (config 3: 26.3 instead of 25.1 ms).
 template <int KL>
 __device__ __forceinline__ void refresh_threshold(EpiState<KL>& st, int kind) {
   if (!st.real) {
@@ -563,8 +568,16 @@ __device__ __forceinline__ void refresh_threshold(EpiState<KL>& st, int kind) {
   if constexpr (KL == 0) {  // append mode: fixed per-query threshold (already has its slack)
     st.thr = s_threshold(st.gw, st.inv_m, st.ta, kind);
   } else {
-    const float own = keys::key_value(st.L[KL - 1]);  // NaN while the list is not full
-    st.thr = s_threshold(fminf(own, st.gw), st.inv_m, st.ta, kind);
+    float w = fminf(keys::key_value(st.L[KL - 1]), st.gw);  // NaN entries: not full yet
+    if (KL == 4 && st.kpub >= 0) {
+      // Branch-free selection keeps the list in registers.
+      uint64_t kth = 0;
+#pragma unroll
+      for (int i = 0; i < KL; ++i) kth |= st.L[i] & (0ull - static_cast<uint64_t>(i == st.kpub));
+      const float kv = keys::key_value(kth);  // NaN while that rank is empty
+      w = fminf(w, kv + (fabsf(kv) + fabsf(st.ta.x) + fabsf(st.ta.y)) * 1e-5f);
+    }
+    st.thr = s_threshold(w, st.inv_m, st.ta, kind);
   }
 }
 
@@ -722,6 +735,7 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
   const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
   uint32_t tile = 0;
   EpiState<KL> st;
+  st.kpub = (p.k_pub >= 1 && p.k_pub <= KL) ? p.k_pub - 1 : -1;
   for (int item = first_item(); item < p.num_items; item += item_step()) {
     const Item it = item_of(p, item, rank);
     const int64_t q = static_cast<int64_t>(it.qt) * kTileQ + quarter * 32 + lane;
