@@ -643,6 +643,7 @@ def run_ours(args, cfg):
                 "metric": cfg["metric"], "rows_per_gpu": hi - lo,
                 "parallelism": f"rows sharded over {world} GPU(s), NCCL all-gather merge"
                 if world > 1 else "1 GPU",
+                **({"peer_bounds": res.peer_bounds()} if world > 1 else {}),
                 "l2": "inputs larger than L2 (database >> 126 MB), no flush needed",
                 "build_s": round(build_s, 3),
                 "phase_ms_mean": [round(statistics.mean(p[i] for p in phases), 4)

@@ -55,6 +55,15 @@ OVVS_API ovvsStatus ovvsResourcesPhaseHistoryMs(ovvsResources_t res, float* ms,
    side slot empty/full), 0x201 the self test below. Not in the reference. */
 OVVS_API ovvsStatus ovvsResourcesLastKernelError(ovvsResources_t res, int32_t* code);
 
+/* 1 when sharded searches on this Resources share each query's bound with the other ranks: the
+   fused kernel of every rank min-writes its current k-th best key for a query into every
+   rank's bound array (mapped over NVLink from a CUDA virtual-memory allocation each rank
+   exports to its peers), so each rank filters with the best bound found on any rank. 0 before
+   the first sharded search, when peer memory cannot be shared, for cosine and large-k searches
+   (which keep their bound on their own rank), or when OVVS_PEER_BOUNDS=0 is set (on every
+   rank). Results are the same either way. Not in the reference. */
+OVVS_API ovvsStatus ovvsResourcesPeerBounds(ovvsResources_t res, int32_t* active);
+
 /* Runs a one-block kernel whose bounded wait is never satisfied, with a limit of `limit_ns`
    nanoseconds (1e6..5e9), and checks that the watchdog fired: the kernel returns, the
    synchronising call reports OVVS_STATUS_ERROR and the code is 0x201. Returns

@@ -116,6 +116,7 @@ def _bind(lib):
         "ovvsResourcesLastPhaseMs": ([c_void_p, P(c_float), c_int32], c_int32),
         "ovvsResourcesPhaseHistoryMs": ([c_void_p, P(c_float), c_int32, P(c_int32)], c_int32),
         "ovvsResourcesLastKernelError": ([c_void_p, P(c_int32)], c_int32),
+        "ovvsResourcesPeerBounds": ([c_void_p, P(c_int32)], c_int32),
         "ovvsWatchdogSelfTest": ([c_void_p, c_int64, P(c_int32)], c_int32),
         "ovvsNcclUniqueIdSize": ([], c_int32),
         "ovvsNcclUniqueId": ([c_void_p, c_int32], c_int32),
@@ -334,6 +335,12 @@ class Resources:
         code = c_int32(0)
         _check(lib().ovvsResourcesLastKernelError(self._h, byref(code)), "last kernel error")
         return code.value
+
+    def peer_bounds(self) -> bool:
+        """Whether sharded searches share each query's bound with the other ranks (peer memory)."""
+        v = c_int32(0)
+        _check(lib().ovvsResourcesPeerBounds(self._h, byref(v)), "peer bounds")
+        return bool(v.value)
 
     def watchdog_self_test(self, limit_ns: int = 50_000_000) -> int:
         """Runs a kernel whose bounded wait is never satisfied; returns the watchdog code (0x201)."""

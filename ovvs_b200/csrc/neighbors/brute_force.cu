@@ -5,6 +5,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <limits>
 #include <vector>
@@ -54,6 +55,10 @@ bool plan_chunks(int dp, int cap, int* nchunk, int* cx, int* cw) {
 }
 
 }  // namespace
+
+// Databases of at most this many 256-row tiles (k-means centroids, coarse quantisers) are
+// filtered on every column's exact ranking value (FusedParams::exact_filter).
+constexpr int kExactFilterTiles = 64;
 
 int list_size_for(int64_t k_eff) {
   const int64_t need = k_eff + std::max<int64_t>(2, (k_eff + 7) / 8);
@@ -268,6 +273,43 @@ namespace {
 
 int launch_grid(const prim::FusedParams& p, int num_sms) {
   return prim::fused_grid(p.num_items, num_sms);
+}
+
+// Sharded list-mode searches: *own = this rank's bound array in the peer window and
+// p.peer_bound = the other ranks' arrays, so the fused kernel shares each query's bound across
+// ranks. The window is created (and grown) here, collectively: every rank of a sharded search
+// reaches this point with the same q_pad. *own stays null when the window is unavailable or
+// switched off with OVVS_PEER_BOUNDS=0 (which must then be set on every rank); the search then
+// keeps its bound on its own rank.
+ovvsStatus peer_bound_arrays(rt::Resources& r, int64_t q_pad, uint64_t** own,
+                             prim::FusedParams& p) {
+  *own = nullptr;
+  if (r.peer_bounds == 0) {
+    const char* e = std::getenv("OVVS_PEER_BOUNDS");
+    if ((e && std::strcmp(e, "0") == 0) || r.world < 2 || r.world - 1 > prim::kMaxPeers)
+      r.peer_bounds = -1;
+  }
+  if (r.peer_bounds < 0) return OVVS_STATUS_SUCCESS;
+  const size_t need = static_cast<size_t>(q_pad) * sizeof(uint64_t);
+  if (!r.bound_win.ready() || r.bound_win.bytes() < need) {
+    // this rank's kernels stop using the old window before it is unmapped
+    if (r.bound_win.ready()) OVVS_TRY(r.finish());
+    const uint64_t tag =
+        r.comm_tag ^ (0x9E3779B97F4A7C15ull * static_cast<uint64_t>(++r.window_seq));
+    const ovvsStatus st =
+        r.bound_win.create(r, std::max(need, size_t(1) << 20), tag, r.nccl_timeout_ms);
+    if (st == OVVS_STATUS_UNSUPPORTED) {
+      r.peer_bounds = -1;
+      return OVVS_STATUS_SUCCESS;
+    }
+    OVVS_TRY(st);
+    r.peer_bounds = 1;
+  }
+  *own = static_cast<uint64_t*>(r.bound_win.ptr(r.rank));
+  p.n_peers = 0;
+  for (int g = 0; g < r.world; ++g)
+    if (g != r.rank) p.peer_bound[p.n_peers++] = static_cast<uint64_t*>(r.bound_win.ptr(g));
+  return OVVS_STATUS_SUCCESS;
 }
 
 // Large k (k plus re-rank margin above the register lists): bound pre-pass on a sample of the
@@ -505,13 +547,16 @@ ovvsStatus search_device(rt::Resources& r, const BruteIndex& ix, const float* d_
                        static_cast<size_t>(c.q_pad) * p.num_sc * prim::kListsPerItem * kl, &cand));
     p.out = cand;
     uint64_t* bound = nullptr;
-    OVVS_TRY(r.scratch(rt::kWsBound, static_cast<size_t>(c.q_pad), &bound));
+    if (ix.sharded && p.rank_kind != prim::kRankColumnScaled)
+      OVVS_TRY(peer_bound_arrays(r, c.q_pad, &bound, p));
+    if (!bound) OVVS_TRY(r.scratch(rt::kWsBound, static_cast<size_t>(c.q_pad), &bound));
     OVVS_TRY_CUDA(cudaMemsetAsync(bound, 0xFF, static_cast<size_t>(c.q_pad) * sizeof(uint64_t), s));
     if (d_init_bound)
       OVVS_TRY_CUDA(cudaMemcpyAsync(bound, d_init_bound, static_cast<size_t>(nq) * sizeof(uint64_t),
                                     cudaMemcpyDeviceToDevice, s));
     p.q_bound = bound;
     p.k_pub = static_cast<int>(k_eff);
+    p.exact_filter = ix.num_tiles <= kExactFilterTiles ? 1 : 0;
     r.mark(1);
     OVVS_TRY_CUDA(prim::launch_knn_fused(c.maps, p, kl, launch_grid(p, pair_sms(r, p)), s));
     r.mark(2);

@@ -549,6 +549,7 @@ struct EpiState {
   uint64_t gkey;  // append mode: the query's bound key
   bool by_key;    // append mode: compare keys (bound value not finite, or exact mode)
   int kpub;       // 4-entry lists: index of the entry that bounds the query (k_pub - 1), or -1
+  bool xf;        // exact filter: thr is a ranking value (candidates: v <= thr), not a bound on s
 };
 
 // Ranking value the filter compares against: the list's own worst entry, tightened by the
@@ -562,7 +563,7 @@ struct EpiState {
 template <int KL>
 __device__ __forceinline__ void refresh_threshold(EpiState<KL>& st, int kind) {
   if (!st.real) {
-    st.thr = kInf;  // padding lanes never select
+    st.thr = st.xf ? -kInf : kInf;  // padding lanes never select
     return;
   }
   if constexpr (KL == 0) {  // append mode: fixed per-query threshold (already has its slack)
@@ -577,7 +578,7 @@ __device__ __forceinline__ void refresh_threshold(EpiState<KL>& st, int kind) {
       const float kv = keys::key_value(kth);  // NaN while that rank is empty
       w = fminf(w, kv + (fabsf(kv) + fabsf(st.ta.x) + fabsf(st.ta.y)) * 1e-5f);
     }
-    st.thr = s_threshold(w, st.inv_m, st.ta, kind);
+    st.thr = st.xf ? w : s_threshold(w, st.inv_m, st.ta, kind);
   }
 }
 
@@ -594,21 +595,29 @@ __device__ __forceinline__ void apply_bound(uint64_t b, EpiState<KL>& st) {
   st.gw = w + mag * 1e-5f;
 }
 
-template <int KL>
-__device__ __forceinline__ void read_bound(const FusedParams& p, int64_t q, EpiState<KL>& st) {
-  apply_bound<KL>(__ldcg(reinterpret_cast<const unsigned long long*>(p.q_bound + q)), st);
+// Min-writes `kth` into every other rank's bound array. Out of line, and compiled only into the
+// kernels of sharded searches: inlined into the epilogue's tile loop (even never executed) it
+// slowed config 3 by 12 %, and as a call by 1.5 %.
+__device__ __noinline__ void publish_to_peers(const FusedParams& p, int64_t q, uint64_t kth) {
+  for (int i = 0; i < p.n_peers; ++i)
+    atomicMin_system(reinterpret_cast<unsigned long long*>(p.peer_bound[i] + q), kth);
 }
 
-template <int KL>
+// `seen` is the bound this lane read last: a key that beats it is news to the other ranks too.
+template <int KL, bool PEER>
 __device__ __forceinline__ void publish_bound(const FusedParams& p, int64_t q,
-                                              const EpiState<KL>& st) {
+                                              const EpiState<KL>& st, uint64_t seen) {
   if (p.k_pub < 1 || p.k_pub > KL) return;  // the list cannot bound that rank
   // Branch-free selection keeps the list in registers (a select chain would be turned into an
   // indexed load, which moves the whole list to local memory).
   uint64_t kth = 0;
 #pragma unroll
   for (int i = 0; i < KL; ++i) kth |= st.L[i] & (0ull - static_cast<uint64_t>(i == p.k_pub - 1));
-  if (kth != kEmptyKey) atomicMin(reinterpret_cast<unsigned long long*>(p.q_bound + q), kth);
+  if (kth == kEmptyKey) return;
+  atomicMin(reinterpret_cast<unsigned long long*>(p.q_bound + q), kth);
+  if constexpr (PEER) {
+    if (kth < seen) publish_to_peers(p, q, kth);
+  }
 }
 
 // r[j] for a run-time j through a tree of selects on statically indexed registers (an indexed
@@ -721,7 +730,65 @@ __device__ __forceinline__ void check_row(const FusedParams& p, const float* row
   }
 }
 
+__device__ __forceinline__ float min32(const float (&r)[32]) {
+  float a[10];
+#pragma unroll
+  for (int i = 0; i < 10; ++i) a[i] = ptx::fmin3(r[3 * i], r[3 * i + 1], r[3 * i + 2]);
+  const float b0 = ptx::fmin3(a[0], a[1], a[2]), b1 = ptx::fmin3(a[3], a[4], a[5]);
+  const float b2 = ptx::fmin3(a[6], a[7], a[8]), b3 = ptx::fmin3(a[9], r[30], r[31]);
+  return fminf(ptx::fmin3(b0, b1, b2), b3);
+}
+
+// Exact filter: turns a chunk's 32 dot products into ranking values in place, with the same
+// arithmetic as the slow path (aux = the chunk's 32 columns in shared memory, 16-byte aligned).
+__device__ __forceinline__ void chunk_values(float (&r)[32], const float* aux, float m, int kind) {
+  if (kind == kRankScaled) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) r[j] = r[j] * m;
+    return;
+  }
+#pragma unroll
+  for (int j4 = 0; j4 < 8; ++j4) {
+    const float4 a = reinterpret_cast<const float4*>(aux)[j4];
+    const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float& v = r[4 * j4 + i];
+      v = kind == kRankAffine ? fmaf(v, m, av[i]) : v * av[i];
+    }
+  }
+}
+
+// Exact filter: the columns of one chunk whose ranking value v (in r) is within the threshold,
+// inserted into the list in column order, re-checked against the threshold as it tightens.
 template <int KL>
+__device__ __forceinline__ void exact_chunk(const FusedParams& p, const float (&r)[32],
+                                            int64_t col0, int ct0, const uint8_t* side,
+                                            EpiState<KL>& st) {
+  const uint32_t* ids = reinterpret_cast<const uint32_t*>(side + kSideIdOff);
+  const uint32_t* allow = reinterpret_cast<const uint32_t*>(side + kSideAllowOff);
+  uint32_t mask = 0;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) mask |= static_cast<uint32_t>(!(r[j] > st.thr)) << j;
+  while (mask) {
+    const int j = __ffs(mask) - 1;
+    mask &= mask - 1;
+    const float v = pick32(r, j);
+    if (v > st.thr) continue;  // threshold tightened by an earlier insertion
+    const int64_t pos = col0 + j;
+    if (pos >= p.n_rows) break;
+    const int ct = ct0 + j;
+    // a row outside the allow list ranks as +inf (it still fills a list that has room)
+    const bool allowed = p.allow == nullptr || ((allow[ct >> 5] >> (ct & 31)) & 1u);
+    const uint64_t key = keys::make_key(allowed ? v : kInf, ids[ct]);
+    if (key < st.L[KL - 1]) {
+      list_insert<KL>(st.L, key);
+      refresh_threshold<KL>(st, p.rank_kind);
+    }
+  }
+}
+
+template <int KL, bool XF, bool PEER>
 __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_base, uint32_t rank) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // TMEM buffers are handed back to the leader's MMA thread: its tempty barrier counts the
@@ -736,6 +803,7 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
   uint32_t tile = 0;
   EpiState<KL> st;
   st.kpub = (p.k_pub >= 1 && p.k_pub <= KL) ? p.k_pub - 1 : -1;
+  st.xf = XF;
   for (int item = first_item(); item < p.num_items; item += item_step()) {
     const Item it = item_of(p, item, rank);
     const int64_t q = static_cast<int64_t>(it.qt) * kTileQ + quarter * 32 + lane;
@@ -753,7 +821,8 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
     float2 ta_pf = make_float2(0.f, 0.f);
     st.ta = p.group_aux[g_cur];
     if constexpr (KL > 0) {
-      read_bound<KL>(p, q, st);
+      bound_pf = __ldcg(reinterpret_cast<const unsigned long long*>(p.q_bound + q));
+      apply_bound<KL>(bound_pf, st);
 #pragma unroll
       for (int i = 0; i < KL; ++i) st.L[i] = kEmptyKey;
     } else {
@@ -783,7 +852,7 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
         if (phase_t == kBoundPeriod - 2 && st.real)
           bound_pf = __ldcg(reinterpret_cast<const unsigned long long*>(p.q_bound + q));
         if (phase_t == kBoundPeriod - 1 && st.real) {
-          publish_bound<KL>(p, q, st);
+          publish_bound<KL, PEER>(p, q, st, bound_pf);
           apply_bound<KL>(bound_pf, st);
           refresh = true;
         }
@@ -820,37 +889,52 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
       // buffer is still held; then the buffer goes back to the MMA, then the deferred row.
       uint32_t flagged = 0;  // chunks this lane must re-read
       int saved = -1;        // chunk index in the deferred row, or -1
-#pragma unroll
-      for (int c = 0; c < nchunks; ++c) {
-        float r0[32];
-        ptx::tmem_ld32(taddr + 32 * c, r0);
-        ptx::tmem_wait_ld();
-        if (!(max32(r0) < st.thr)) {
-          if (saved < 0) {
-            uint32_t cand = 0;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              my_row[j] = r0[j];
-              cand |= static_cast<uint32_t>(!(r0[j] < st.thr)) << j;
-            }
-            my_row[32] = __uint_as_float(cand);
-            saved = c;
-          } else {
-            flagged |= 1u << c;
-          }
-        }
-        __syncwarp();
-      }
-      if (__any_sync(0xffffffffu, flagged != 0)) {
+      if constexpr (XF) {
+        // Exact filter: every column's ranking value against the list's threshold; the few
+        // candidates are inserted before the buffer is handed back.
+        const float* aux = reinterpret_cast<const float*>(side + kSideAuxOff) + ct0;
+#pragma unroll 1
         for (int c = 0; c < nchunks; ++c) {
-          if (!__any_sync(0xffffffffu, (flagged >> c) & 1u)) continue;
           float r0[32];
           ptx::tmem_ld32(taddr + 32 * c, r0);
           ptx::tmem_wait_ld();
-          if ((flagged >> c) & 1u) slow_path<KL>(p, r0, col0 + 32 * c, ct0 + 32 * c, side, st);
+          chunk_values(r0, aux + 32 * c, st.m, p.rank_kind);
+          if (!(min32(r0) > st.thr)) exact_chunk<KL>(p, r0, col0 + 32 * c, ct0 + 32 * c, side, st);
           __syncwarp();
         }
-      }
+      } else {
+#pragma unroll
+        for (int c = 0; c < nchunks; ++c) {
+          float r0[32];
+          ptx::tmem_ld32(taddr + 32 * c, r0);
+          ptx::tmem_wait_ld();
+          if (!(max32(r0) < st.thr)) {
+            if (saved < 0) {
+              uint32_t cand = 0;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                my_row[j] = r0[j];
+                cand |= static_cast<uint32_t>(!(r0[j] < st.thr)) << j;
+              }
+              my_row[32] = __uint_as_float(cand);
+              saved = c;
+            } else {
+              flagged |= 1u << c;
+            }
+          }
+          __syncwarp();
+        }
+        if (__any_sync(0xffffffffu, flagged != 0)) {
+          for (int c = 0; c < nchunks; ++c) {
+            if (!__any_sync(0xffffffffu, (flagged >> c) & 1u)) continue;
+            float r0[32];
+            ptx::tmem_ld32(taddr + 32 * c, r0);
+            ptx::tmem_wait_ld();
+            if ((flagged >> c) & 1u) slow_path<KL>(p, r0, col0 + 32 * c, ct0 + 32 * c, side, st);
+            __syncwarp();
+          }
+        }
+      }  // exact filter or conservative bound
       // Every chunk of this warp is read: hand its share of the buffer back.
       ptx::tc_fence_before();
       __syncwarp();
@@ -864,7 +948,7 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
     }
     if (!ok) return;
     if constexpr (KL > 0) {
-      if (st.real) publish_bound<KL>(p, q, st);
+      if (st.real) publish_bound<KL, PEER>(p, q, st, bound_pf);
       uint64_t* dst =
           p.out + ((static_cast<size_t>(q) * p.num_sc + it.sc) * kListsPerItem + part) * KL;
 #pragma unroll
@@ -873,7 +957,7 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
   }
 }
 
-template <int KL>
+template <int KL, bool XF, bool PEER>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFusedThreads, 1)
     knn_fused_kernel(const __grid_constant__ FusedMaps maps, const __grid_constant__ FusedParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -931,7 +1015,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFusedThreads, 1)
     }
     __syncwarp();
   } else {
-    run_epilogue<KL>(p, s, tmem_base, rank);
+    run_epilogue<KL, XF, PEER>(p, s, tmem_base, rank);
   }
 
   // The leader's MMAs read the other CTA's shared memory and write its TMEM: that CTA waits for
@@ -950,9 +1034,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFusedThreads, 1)
   }
 }
 
-template <int KL>
+template <int KL, bool XF = false, bool PEER = false>
 cudaError_t launch_kl(const FusedMaps& maps, const FusedParams& p, int grid, cudaStream_t stream) {
-  auto kern = knn_fused_kernel<KL>;
+  auto kern = knn_fused_kernel<KL, XF, PEER>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem_bytes);
   if (e != cudaSuccess) return e;
   kern<<<grid, kFusedThreads, p.smem_bytes, stream>>>(maps, p);
@@ -970,7 +1054,7 @@ int fused_max_pairs(int smem_bytes) {
   const auto key = std::make_pair(dev, smem_bytes);
   auto hit = cache.find(key);
   if (hit != cache.end()) return hit->second;
-  auto kern = knn_fused_kernel<16>;  // every instance has the same threads, smem and cluster shape
+  auto kern = knn_fused_kernel<16, false, false>;  // every instance: same threads, smem, cluster
   int pairs = 0;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) ==
       cudaSuccess) {
@@ -1046,6 +1130,34 @@ bool plan_fused_smem(FusedParams& p, int max_smem_optin) {
 
 cudaError_t launch_knn_fused(const FusedMaps& maps, const FusedParams& p, int kl, int grid,
                              cudaStream_t stream) {
+  if (p.n_peers > 0) {  // sharded search sharing its bounds (list mode, conservative filter)
+    switch (kl) {
+      case 4:
+        return launch_kl<4, false, true>(maps, p, grid, stream);
+      case 8:
+        return launch_kl<8, false, true>(maps, p, grid, stream);
+      case 12:
+        return launch_kl<12, false, true>(maps, p, grid, stream);
+      case 16:
+        return launch_kl<16, false, true>(maps, p, grid, stream);
+      case 32:
+        return launch_kl<32, false, true>(maps, p, grid, stream);
+      default:
+        break;  // append mode has no lists to publish
+    }
+  }
+  if (p.exact_filter && p.rank_kind != kRankScaled) {
+    switch (kl) {
+      case 4:
+        return launch_kl<4, true>(maps, p, grid, stream);
+      case 8:
+        return launch_kl<8, true>(maps, p, grid, stream);
+      case 12:
+        return launch_kl<12, true>(maps, p, grid, stream);
+      default:
+        break;  // longer lists: the conservative filter
+    }
+  }
   switch (kl) {
     case 4:
       return launch_kl<4>(maps, p, grid, stream);

@@ -62,6 +62,7 @@ constexpr int kMaxStages = 16;             // smem ring slots at most
 constexpr int kMaxChunks = 66;             // padded dim <= 4096 per part (64 + 32/16 tails)
 constexpr int kResChunks = 8;              // resident query tile: at most 8 chunks per part
 constexpr int kTmemCols = 512;             // two 256-column fp32 accumulators
+constexpr int kMaxPeers = 15;              // other ranks a sharded search shares bounds with
 constexpr int kSideBufs = 4;               // side ring depth (tiles)
 constexpr int kSideAuxOff = 0;             // side slot: aux[256] fp32
 constexpr int kSideIdOff = 1024;           //            row id[256] u32
@@ -126,6 +127,18 @@ struct FusedParams {
   int64_t nq;                      // real queries (lanes >= nq are padding and never select)
   int k_pub;                       // rank (1-based) whose key a list publishes as a bound
   uint64_t* q_bound;               // [q_pad] smallest published k_pub-th key per query
+  // Sharded searches: the q_bound arrays of the other ranks, mapped from their GPUs. A list
+  // whose k_pub-th key beats the bound it last read also min-writes it there, so every rank
+  // filters with the best bound found on any rank (rank values are in the same units on every
+  // rank: not used for cosine, whose values carry each shard's scale).
+  uint64_t* peer_bound[kMaxPeers] = {};
+  int n_peers = 0;
+  // List mode, L2 / cosine over few rows (k-means centroids, coarse quantisers): the filter
+  // compares every column's ranking value with the list's threshold instead of the tile group's
+  // conservative bound on s. Rows are sorted by aux, but a group of 8 tiles of a small database
+  // spans a wide aux range, so the conservative bound lets many columns through to the exact
+  // path; computing each value (one FMA per column with aux from shared memory) costs less.
+  int exact_filter = 0;
   uint64_t* out;                   // [q_pad][num_sc][kListsPerItem][KL] sorted keys (list mode;
                                    // one list per column part)
   int* err;                        // watchdog word

@@ -276,5 +276,12 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
+// Three-input fp32 min (sm_100): NaN operands are ignored unless all are NaN.
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 }  // namespace ptx
 }  // namespace ovvs

@@ -529,6 +529,16 @@ ovvsStatus ovvsResourcesLastKernelError(ovvsResources_t res, int32_t* code) {
   return OVVS_STATUS_SUCCESS;
 }
 
+ovvsStatus ovvsResourcesPeerBounds(ovvsResources_t res, int32_t* active) {
+  if (!res || !active) return OVVS_STATUS_INVALID_ARGUMENT;
+  Resources& r = *from_handle(res);
+  std::lock_guard<std::mutex> lk(r.mu);
+  // A one-process group reports its members (they share bounds with each other or none do).
+  const Resources& m = r.group.empty() ? r : *r.group.front();
+  *active = m.peer_bounds == 1 ? 1 : 0;
+  return OVVS_STATUS_SUCCESS;
+}
+
 ovvsStatus ovvsWatchdogSelfTest(ovvsResources_t res, int64_t limit_ns, int32_t* code) {
   if (!res || !code || limit_ns < 1000000 || limit_ns > 5000000000LL)
     return OVVS_STATUS_INVALID_ARGUMENT;

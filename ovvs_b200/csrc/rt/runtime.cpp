@@ -108,6 +108,13 @@ void short_pause() { std::this_thread::sleep_for(std::chrono::microseconds(50));
 ovvsStatus init_comm(Resources& r, const ncclUniqueId& id) {
   const NcclApi* nc = nccl();
   if (!nc) return OVVS_STATUS_DEVICE_UNAVAILABLE;
+  // FNV-1a of the unique id: the same on every rank, different for every communicator.
+  uint64_t h = 1469598103934665603ull;
+  for (size_t i = 0; i < sizeof(id.internal); ++i) {
+    h ^= static_cast<uint8_t>(id.internal[i]);
+    h *= 1099511628211ull;
+  }
+  r.comm_tag = h;
   ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
   cfg.blocking = 0;
   const ncclResult_t ret = nc->CommInitRankConfig(&r.comm, r.world, id, r.rank, &cfg);
@@ -177,10 +184,14 @@ Resources::~Resources() {
   if (abort_pending) {
     // A collective of the aborted communicator may still run: freeing could wait on it.
     for (auto& b : ws) b.abandon();
+    bound_win.abandon();
     d_err = nullptr;
     stage_buf[0] = stage_buf[1] = nullptr;
   }
   if (gpu_available) cudaSetDevice(device);
+  // The peer window is unmapped only once this rank's kernels are done with it.
+  if (bound_win.ready() && stream) cudaStreamSynchronize(stream);
+  bound_win.reset();
   for (auto& b : ws) b.release();
   if (comm) ovvs::rt::nccl()->CommDestroy(comm);
   if (d_err) cudaFree(d_err);

@@ -21,6 +21,7 @@
 
 #include "nccl_dl.hpp"
 #include "ovvs/ovvs.h"
+#include "peer_window.hpp"
 
 struct ovvsResourcesImpl;
 
@@ -139,6 +140,13 @@ struct Resources {
   // occupy the device, so this Resources leaves its device memory to the process's exit.
   bool abort_pending = false;
   int64_t nccl_timeout_ms = 60000; // deadline of NCCL set-up and of waits on collectives
+  uint64_t comm_tag = 0;           // hash of the communicator's unique id (same on every rank)
+  int window_seq = 0;              // peer windows created so far (names their exchanges)
+  // Sharded searches share each query's bound between ranks through this window (q_pad keys
+  // per rank). peer_bounds: 0 not tried yet, 1 in use, -1 unavailable or switched off
+  // (OVVS_PEER_BOUNDS=0).
+  PeerWindow bound_win;
+  int peer_bounds = 0;
   // One process, several devices (ovvsResourcesCreate with OVVS_CUDA_DEVICES naming more than
   // one): this object is an ordinary Resources on the first device, and `group` holds one member
   // per device (rank g of world G, sharing a communicator) driven by one worker thread each.

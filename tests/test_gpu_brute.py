@@ -181,6 +181,21 @@ def test_bitset_filtering(ovvs, gpu, oracle):
                     bitset=bs)
 
 
+@pytest.mark.parametrize("n", [9000, 40_000])
+@pytest.mark.parametrize("metric", ["l2", "cosine", "l2_sqrt"])
+@pytest.mark.parametrize("k", [1, 10])
+def test_both_filters(n, metric, k, ovvs, gpu, oracle):
+    """Databases of at most 64 tiles (16,384 rows) filter on every column's exact ranking value;
+    larger ones on the tile group's conservative bound on the dot product. Both, with and
+    without an allow list, against the oracle."""
+    rng = np.random.default_rng(n + k)
+    _run_parity(ovvs, gpu, oracle, metric, "f32", n=n, dim=32, nq=96, k=k, seed=n + k,
+                kind="mixture")
+    bs = ovvs.bitset_from_allow_list(n, np.nonzero(rng.random(n) < 0.02)[0])
+    _run_parity(ovvs, gpu, oracle, metric, "f32", n=n, dim=32, nq=96, k=k, seed=n + k,
+                kind="mixture", bitset=bs)
+
+
 def test_duplicates_tie_by_lower_id(ovvs, gpu, oracle):
     rng = np.random.default_rng(9)
     base = rng.standard_normal((50, 16)).astype(np.float32)

@@ -40,12 +40,13 @@ def _worker(rank, world, uid, out):
         lo, hi = row_range(rank, world, N)
         ix = ov.BruteIndex.build(data[lo:hi], metric="l2", resources=res, row_offset=lo)
         nb, dist = ix.search(queries, K)
+        peer = res.peer_bounds()  # the ranks shared their query bounds through peer memory
         klo, khi = row_range(rank, world, KM_N)
         model = ov.KMeans(km[klo:khi], nclusters=KM_K, iters=KM_ITERS, resources=res,
                           row_offset=klo, n_total=KM_N)
-        out.put((rank, np.asarray(nb), np.asarray(dist), model.centroids(), None))
+        out.put((rank, np.asarray(nb), np.asarray(dist), model.centroids(), peer, None))
     except Exception as e:  # reported to the parent instead of hanging it
-        out.put((rank, None, None, None, repr(e)))
+        out.put((rank, None, None, None, None, repr(e)))
 
 
 def test_two_gpu_shards_match_one_gpu(ovvs, gpu):
@@ -62,8 +63,9 @@ def test_two_gpu_shards_match_one_gpu(ovvs, gpu):
     try:
         got = {}
         for _ in range(2):
-            rank, nb, dist, cent, err = out.get(timeout=300)
+            rank, nb, dist, cent, peer, err = out.get(timeout=300)
             assert err is None, f"rank {rank}: {err}"
+            assert peer, f"rank {rank}: sharded search did not share bounds through peer memory"
             got[rank] = (nb, dist, cent)
         for p in procs:
             p.join(timeout=60)
@@ -97,17 +99,18 @@ def _group_worker(out):
         res = ov.Resources()
         ix = ov.BruteIndex.build(data, metric="l2", resources=res)
         nb, dist = ix.search(queries, K)
+        peer = res.peer_bounds()
         ip = ov.BruteIndex.build(data, metric="inner_product", resources=res)
         bits = ov.bitset_from_allow_list(N, np.arange(0, N, 3))
         nb_ip, dist_ip = ip.search(queries, 25, bitset=bits)
         model = ov.KMeans(km, nclusters=KM_K, iters=KM_ITERS, resources=res)
         labels, _ = model.predict(km)
         out.put((np.asarray(nb), np.asarray(dist), np.asarray(nb_ip), np.asarray(dist_ip),
-                 model.centroids(), np.asarray(labels), res.last_device(), None))
+                 model.centroids(), np.asarray(labels), res.last_device(), peer, None))
         for o in (ix, ip, model, res):
             o.close()
     except Exception as e:
-        out.put((None,) * 7 + (repr(e),))
+        out.put((None,) * 8 + (repr(e),))
 
 
 def test_plain_abi_over_two_gpus(ovvs, gpu, oracle):
@@ -123,8 +126,9 @@ def test_plain_abi_over_two_gpus(ovvs, gpu, oracle):
     p = ctx.Process(target=_group_worker, args=(out,))
     p.start()
     try:
-        nb, dist, nb_ip, dist_ip, cent, labels, last, err = out.get(timeout=300)
+        nb, dist, nb_ip, dist_ip, cent, labels, last, peer, err = out.get(timeout=300)
         assert err is None, err
+        assert peer, "the two GPUs' shards did not share query bounds through peer memory"
         p.join(timeout=60)
         assert p.exitcode == 0
     finally:
@@ -162,6 +166,10 @@ def _leaving_worker(rank, uid, out, go, log_path):
 
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     os.environ["OVVS_NCCL_TIMEOUT_MS"] = "10000"
+    # The surviving rank's next fused kernel would write its query bounds into the departed
+    # rank's bound array (memory this process keeps mapped, so it stays allocated); this test
+    # keeps to NCCL and plain device memory and leaves that case out.
+    os.environ["OVVS_PEER_BOUNDS"] = "0"
 
     def leave(msg):
         out.put(msg)
