@@ -73,6 +73,14 @@ CONFIGS = {
                 nlist=1024, nprobe=32, dist="mixture", centres=1024, centre_std=2.0, seed=5,
                 desc="IVF-Flat L2 fp32, N=1M x 128 Gaussian mixture (1024 centres, var 4), "
                      "nlist=1024, nprobe=32, Q=10k, k=10"),
+    # the dense primitives (ovvsPairwiseDistance / ovvsGemm, host buffers in and out): one step =
+    # one call over a [nx x dim] x [ny x dim] problem whose output block fits one launch
+    "pw": dict(kind="prim", op="pairwise", metric="l2", nx=4096, ny=65536, dim=128,
+               dist="mixture", centres=1024, centre_std=2.0, seed=6,
+               desc="ovvsPairwiseDistance L2 fp32, 4096 x 65536 pairs, D=128"),
+    "gemm": dict(kind="prim", op="gemm", nx=4096, ny=65536, dim=128, dist="mixture",
+                 centres=1024, centre_std=2.0, seed=7,
+                 desc="ovvsGemm fp32, C[4096 x 65536] = A[4096 x 128] B[65536 x 128]^T"),
     # k-means (ovvsKMeansFit): one step = one full fit of `iters` Lloyd iterations
     "c4": dict(kind="kmeans", metric="l2", dtype="f32", n=5_000_000, dim=128, clusters=4096,
                iters=10, dist="mixture", centres=4096, centre_std=3.0, seed=3,
@@ -1092,6 +1100,189 @@ def run_ivf_reference(args, cfg):
     return 0
 
 
+def _prim_data(cfg):
+    """Host operands of a primitive config (seeded mixture rows, fp32)."""
+    rng = np.random.default_rng(cfg["seed"])
+    centres = rng.normal(0, cfg["centre_std"], (cfg["centres"], cfg["dim"])).astype(np.float32)
+
+    def rows(n):
+        return (centres[rng.integers(0, cfg["centres"], n)]
+                + rng.standard_normal((n, cfg["dim"]), dtype=np.float32)).astype(np.float32)
+
+    return rows(cfg["nx"]), rows(cfg["ny"])
+
+
+def _prim_metric(cfg):
+    return (f"{cfg['op']} outputs/sec @ {cfg['nx']} x {cfg['ny']} x D={cfg['dim']} fp32"
+            + (f" {cfg['metric']}" if cfg["op"] == "pairwise" else ""))
+
+
+def _prim_call(obj, cfg, x, y):
+    """One call of the config's primitive through the C ABI: `obj` is this library's Resources or
+    the reference library's wrapper (oracle.cpu.Reference)."""
+    if cfg["op"] == "gemm":
+        return obj.gemm(x, y, x.shape[0], y.shape[0], x.shape[1], 1)
+    if hasattr(obj, "pairwise_distance"):  # this library
+        return obj.pairwise_distance(x, y, cfg["metric"])
+    return obj.pairwise(cfg["metric"], x, y)  # the reference
+
+
+def _prim_reference_rows(cfg, seconds):
+    rate = 2.1e9  # reference naive fp32 GEMM, FLOP/s on one thread (measured on C1)
+    return max(1, min(cfg["nx"], int(seconds * rate / (2.0 * cfg["ny"] * cfg["dim"]))))
+
+
+def run_prim(args, cfg):
+    """Dense primitive arm (one GPU; with --gpus N each rank is an independent replica). `value` =
+    outputs per second of the kernels alone (phase [1] of the call, CUDA events on the library's
+    stream: row norms, the sequential fp32 GEMM and the metric epilogue for the whole output,
+    which fits one block); `e2e` = the same calls with the host copies (operands in, the nx x ny
+    output back), CUDA events around each call. The kernels keep the reference's sequential fp32
+    operation order (bit-identical results), so they run on the CUDA cores: the roofline is the
+    FP32 issue rate (one instruction per flop: separately rounded multiply and add)."""
+    import torch
+    import torch.distributed as dist
+
+    import ovvs_b200 as ov
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    res = ov.Resources.sharded(local, 0, 1, None)
+    x, y = _prim_data(cfg)
+    nx, ny, dim = cfg["nx"], cfg["ny"], cfg["dim"]
+    out = None
+    for _ in range(args.warmup):
+        out = _prim_call(res, cfg, x, y)
+    stream = torch.cuda.ExternalStream(res.stream(), device=dev)
+    res.set_profiling(True)
+    kern, e2e = [], []
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(local) as clocks:
+        for _ in range(args.steps):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            out = _prim_call(res, cfg, x, y)
+            e1.record(stream)
+            e1.synchronize()
+            kern.append(res.last_phase_ms()[1])
+            e2e.append(e0.elapsed_time(e1))
+    res.set_profiling(False)
+    clk = clocks.summary()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    kern_ms = max_over_ranks(statistics.mean(kern))
+    e2e_ms = max_over_ranks(statistics.mean(e2e))
+    flops = 2.0 * nx * ny * dim
+    sm_mhz = clk["sm_mhz"] or 1965.0
+    peak = 128 * torch.cuda.get_device_properties(dev).multi_processor_count * sm_mhz / 1e6
+    achieved = flops / (kern_ms / 1e3) / 1e12
+    line = None
+    if rank == 0:
+        line = {
+            "metric": _prim_metric(cfg), "value": world * nx * ny / (kern_ms / 1e3),
+            "unit": "outputs/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": kern_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{args.config}: {cfg['desc']}", "nx": nx, "ny": ny,
+                       "dim": dim, "parallelism": "1 GPU" if world == 1 else
+                       f"{world} independent replicas (the primitives are not sharded)",
+                       "l2": "output 1 GiB >> 126 MB L2, no flush needed",
+                       "e2e_ms_per_step": e2e_ms},
+            "e2e": {"value": world * nx * ny / (e2e_ms / 1e3), "unit": "outputs/s",
+                    "h2d_bytes_per_step": (nx + ny) * dim * 4, "d2h_bytes_per_step": nx * ny * 4},
+            "gpu_launches": (4 if cfg["op"] == "pairwise" else 1) * args.steps,
+            "roofline": {"bound": "fp32", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "kernel": "gemm_seq_kernel" + (" + norms + pairwise_expand"
+                                                        if cfg["op"] == "pairwise" else ""),
+                         "flops_per_launch": flops,
+                         "note": "sequential fp32 sums in the reference's order on the CUDA "
+                                 "cores; peak = 128 FP32 lanes x SMs x median SM clock, one "
+                                 "instruction per flop"},
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"],
+                       "reasons": clk["reasons"]},
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            from oracle.cpu import Reference
+
+            ref = Reference()
+            rows = _prim_reference_rows(cfg, args.ref_seconds)
+            xs = np.ascontiguousarray(x[:rows])
+            t0 = time.perf_counter()
+            ref_out = np.asarray(_prim_call(ref, cfg, xs, y), np.float32).reshape(rows, ny)
+            secs = time.perf_counter() - t0
+            line["cpu_baseline"] = {
+                "value": rows * ny / secs, "unit": "outputs/s", "cores": 1, "kind": "reference",
+                "sample": f"{rows} of {nx} rows x all {ny} through the reference library built "
+                          "from its sources (oracle/_ref), FORCE_CPU (its naive loop is "
+                          "single-threaded)"}
+            got = np.asarray(out, np.float32).reshape(nx, ny)[:rows]
+            same = got.view(np.uint32) == ref_out.view(np.uint32)
+            line["parity"] = {"rows": rows, "outputs": int(same.size),
+                              "bit_identical": int(same.sum()), "ok": bool(same.all()),
+                              "against": "the reference library (oracle/_ref), FORCE_CPU"}
+    res.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+        if "parity" in line and not line["parity"]["ok"]:
+            return 1
+    return 0
+
+
+def run_prim_reference(args, cfg):
+    """--impl reference for a primitive config: the reference's own ovvsPairwiseDistance /
+    ovvsGemm (FORCE_CPU, single-threaded naive loop) on a row sample of the same operands, in
+    outputs per second."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from oracle.cpu import Reference
+
+    ref = Reference()
+    x, y = _prim_data(cfg)
+    rows = _prim_reference_rows(cfg, args.ref_seconds / max(1, args.steps))
+    xs = np.ascontiguousarray(x[:rows])
+    _prim_call(ref, cfg, xs[:max(1, rows // 8)], y)
+    secs = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        _prim_call(ref, cfg, xs, y)
+        secs.append(time.perf_counter() - t0)
+    value = rows * cfg["ny"] / statistics.mean(secs)
+    sample = (f"{rows} of {cfg['nx']} rows x all {cfg['ny']} per step, FORCE_CPU, 1 thread "
+              "(the reference's naive loop)")
+    line = {"metric": _prim_metric(cfg), "value": value, "unit": "outputs/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * statistics.mean(secs), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference", "config": {"workload": f"{args.config}: {cfg['desc']}",
+                                            "sample": sample},
+            "cpu_baseline": {"value": value, "unit": "outputs/s", "cores": 1,
+                             "kind": "reference", "sample": sample},
+            "e2e": {"value": value, "unit": "outputs/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1110,11 +1301,15 @@ def main():
     if args.impl == "reference":
         if cfg.get("kind") == "ivf":
             return run_ivf_reference(args, cfg)
+        if cfg.get("kind") == "prim":
+            return run_prim_reference(args, cfg)
         return run_reference_arm(args, cfg)
     if cfg.get("kind") == "kmeans":
         return run_kmeans(args, cfg)
     if cfg.get("kind") == "ivf":
         return run_ivf(args, cfg)
+    if cfg.get("kind") == "prim":
+        return run_prim(args, cfg)
     return run_ours(args, cfg)
 
 

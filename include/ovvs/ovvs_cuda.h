@@ -32,7 +32,10 @@ OVVS_API ovvsStatus ovvsResourcesDevice(ovvsResources_t res, int32_t* device);
    up to `count` durations in milliseconds: [0] query preparation (+ allow bits), [1] fused
    distance / top-k kernel, [2] candidate merge + exact re-rank, [3] cross-shard all-gather and
    merge (0 on one GPU). After a k-means fit the phases are the fit's: [0] dataset upload and
-   seeding, [1] the Lloyd iterations, [2] centroid download, [3] 0. */
+   seeding, [1] the Lloyd iterations, [2] centroid download, [3] 0. After ovvsGemm / ovvsGemmEx /
+   ovvsPairwiseDistance: [0] the uploads before the first output block's kernels, [1] those
+   kernels (the whole call when the output fits one block, 1 GiB), [2] the rest (downloads and
+   any further blocks), [3] 0. */
 OVVS_API ovvsStatus ovvsResourcesSetProfiling(ovvsResources_t res, int32_t enable);
 OVVS_API ovvsStatus ovvsResourcesLastPhaseMs(ovvsResources_t res, float* ms, int32_t count);
 

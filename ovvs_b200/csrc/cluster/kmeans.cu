@@ -36,24 +36,40 @@ __global__ void label_keys_kernel(const int64_t* __restrict__ labels, int64_t n,
 __global__ void kmeans_bound_kernel(const float* __restrict__ x, const int64_t* __restrict__ labels,
                                     const float* __restrict__ centroids, int dim, int64_t n,
                                     uint64_t* __restrict__ bound) {
-  const int lane = threadIdx.x & 31;
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (i >= n) return;
-  const int64_t lab = labels[i];
-  const float* xr = x + i * dim;
+  // Four points per warp, eight lanes per point; with rows 16-byte aligned (dim % 4 == 0) each
+  // lane reads its columns four at a time, so a warp has eight 16-byte loads in flight per lane.
+  const int lane = threadIdx.x & 31, sub = lane & 7;
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 4 +
+                    (lane >> 3);
+  const bool active = i < n;
+  const int64_t lab = active ? labels[i] : -1;
+  const float* xr = x + (active ? i : 0) * dim;
   const float* cr = centroids + (lab < 0 ? 0 : lab) * dim;
   float ip = 0.f, yn = 0.f;
-  for (int d = lane; d < dim; d += 32) {
-    const float c = cr[d];
-    ip = fmaf(xr[d], c, ip);
-    yn = fmaf(c, c, yn);
+  if (active) {
+    if ((dim & 3) == 0) {
+      const float4* x4 = reinterpret_cast<const float4*>(xr);
+      const float4* c4 = reinterpret_cast<const float4*>(cr);
+#pragma unroll 4
+      for (int f = sub; f < dim / 4; f += 8) {
+        const float4 a = __ldg(x4 + f), c = c4[f];
+        ip = fmaf(a.x, c.x, fmaf(a.y, c.y, fmaf(a.z, c.z, fmaf(a.w, c.w, ip))));
+        yn = fmaf(c.x, c.x, fmaf(c.y, c.y, fmaf(c.z, c.z, fmaf(c.w, c.w, yn))));
+      }
+    } else {
+      for (int d = sub; d < dim; d += 8) {
+        const float c = cr[d];
+        ip = fmaf(xr[d], c, ip);
+        yn = fmaf(c, c, yn);
+      }
+    }
   }
 #pragma unroll
-  for (int off = 16; off; off >>= 1) {
+  for (int off = 4; off; off >>= 1) {
     ip += __shfl_xor_sync(0xffffffffu, ip, off);
     yn += __shfl_xor_sync(0xffffffffu, yn, off);
   }
-  if (lane == 0) {
+  if (active && sub == 0) {
     const float v = yn - 2.f * ip;
     const float margin = 1e-4f * (fabsf(yn) + 2.f * fabsf(ip)) + 1e-30f;
     const bool ok = lab >= 0 && v == v && fabsf(v) < __int_as_float(0x7f800000);
@@ -64,9 +80,10 @@ __global__ void kmeans_bound_kernel(const float* __restrict__ x, const int64_t* 
 // mixer.cpp:902-918: per centroid, fp32 sum of its rows in ascending row order, then
 // centroid = sum * (1 / count); a centroid without rows keeps its previous value. One block per
 // centroid, one thread per dimension; the cluster's row ids are staged in shared memory 256 at a
-// time so that each thread keeps 8 independent row loads in flight (the additions stay in row
-// order).
+// time so that each thread keeps kUpdateDepth independent row loads in flight (the additions stay
+// in row order).
 constexpr int kUpdateIdx = 256;
+constexpr int kUpdateDepth = 16;
 
 __global__ void centroid_update_kernel(const float* __restrict__ x, int dim,
                                        const uint32_t* __restrict__ sorted_idx,
@@ -89,12 +106,13 @@ __global__ void centroid_update_kernel(const float* __restrict__ x, int dim,
       __syncthreads();
       if (d < dim) {
         int j = 0;
-        for (; j + 8 <= m; j += 8) {
-          float v[8];
+        for (; j + kUpdateDepth <= m; j += kUpdateDepth) {
+          float v[kUpdateDepth];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) v[u] = x[static_cast<int64_t>(s_idx[j + u]) * dim + d];
+          for (int u = 0; u < kUpdateDepth; ++u)
+            v[u] = __ldg(x + static_cast<int64_t>(s_idx[j + u]) * dim + d);
 #pragma unroll
-          for (int u = 0; u < 8; ++u) s = __fadd_rn(s, v[u]);
+          for (int u = 0; u < kUpdateDepth; ++u) s = __fadd_rn(s, v[u]);
         }
         for (; j < m; ++j) s = __fadd_rn(s, x[static_cast<int64_t>(s_idx[j]) * dim + d]);
       }
@@ -124,12 +142,13 @@ __global__ void centroid_partial_kernel(const float* __restrict__ x, int dim,
       __syncthreads();
       if (d < dim) {
         int j = 0;
-        for (; j + 8 <= m; j += 8) {
-          float v[8];
+        for (; j + kUpdateDepth <= m; j += kUpdateDepth) {
+          float v[kUpdateDepth];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) v[u] = x[static_cast<int64_t>(s_idx[j + u]) * dim + d];
+          for (int u = 0; u < kUpdateDepth; ++u)
+            v[u] = __ldg(x + static_cast<int64_t>(s_idx[j + u]) * dim + d);
 #pragma unroll
-          for (int u = 0; u < 8; ++u) s += v[u];
+          for (int u = 0; u < kUpdateDepth; ++u) s += v[u];
         }
         for (; j < m; ++j) s += x[static_cast<int64_t>(s_idx[j]) * dim + d];
       }
@@ -239,7 +258,7 @@ ovvsStatus fit(rt::Resources& r, const float* x, int64_t n_local, int64_t row_of
     int64_t k_eff = 0;
     // From the second iteration on, each point's previous centroid bounds its assignment.
     if (it > 0 && n > 0) {
-      kmeans_bound_kernel<<<static_cast<unsigned>((n + 7) / 8), 256, 0, s>>>(
+      kmeans_bound_kernel<<<static_cast<unsigned>((n + 31) / 32), 256, 0, s>>>(
           m.d_x.as<float>(), m.labels.as<int64_t>(), m.d_centroids.as<float>(),
           static_cast<int>(dim), n, m.bound_keys.as<uint64_t>());
       OVVS_TRY_CUDA(cudaGetLastError());

@@ -133,13 +133,40 @@ __device__ float exact_rank(const MergeParams& p, const float* __restrict__ x, f
   return exact_rank_with(p, x, xn, pos, [&](int d) { return __half2float(y16[d]); });
 }
 
+// The k = 1 assignment's shortcut (labels_only): when the best candidate's approximate value is
+// below the second's by more than their error bound, the best id is the exact argmin. The
+// approximate ranking values v = |y|^2 - 2 x.y differ from the exact ones by at most ~1e-6
+// (|x| |y| + |v|) (split fp16 products, fp32 sums); the margin is 10x wider, so ties never take
+// it. Writes the result and returns true when it applies.
+__device__ __forceinline__ bool assign_shortcut(const MergeParams& p, int64_t q, float xn,
+                                                uint64_t k0, uint64_t k1) {
+  if (k0 == kEmptyKey) return false;
+  const float v0 = keys::key_value(k0);
+  const float v1 = k1 == kEmptyKey ? __int_as_float(0x7f800000) : keys::key_value(k1);
+  const float yn0 = p.norm_sorted[p.inv_perm[keys::key_id(k0)]];
+  const float yn1 = k1 == kEmptyKey ? 0.f : p.norm_sorted[p.inv_perm[keys::key_id(k1)]];
+  const float fin = __int_as_float(0x7f800000);
+  const bool finite = fabsf(v0) < fin && fabsf(xn) < fin && fabsf(yn0) < fin &&
+                      fabsf(yn1) < fin && !(v1 != v1);
+  const float margin =
+      1e-5f * (fabsf(v0) + (k1 == kEmptyKey ? 0.f : fabsf(v1)) + xn + yn0 + yn1 +
+               2.f * sqrtf(xn * yn0) + 2.f * sqrtf(xn * yn1)) + 1e-30f;
+  if (!(finite && v1 - v0 > margin)) return false;
+  p.neighbors[q] = p.row_offset + static_cast<int64_t>(keys::key_id(k0));
+  p.distances[q] = __fadd_rn(xn, v0);
+  return true;
+}
+
+__host__ __device__ inline bool use_assign_shortcut(const MergeParams& p) {
+  return p.labels_only && p.k_eff == 1 && p.neighbors && p.allow == nullptr &&
+         p.metric == kMetricL2;
+}
+
+// Merge + exact re-rank of query q by one warp (lists: this warp's KL x 32 keys of shared
+// memory).
 template <int KL>
-__global__ void __launch_bounds__(kMergeWarps * 32)
-    merge_rerank_kernel(const MergeParams p) {
-  extern __shared__ uint64_t merge_smem[];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t q = static_cast<int64_t>(blockIdx.x) * kMergeWarps + warp;
-  if (q >= p.nq) return;
+__device__ void merge_query(const MergeParams& p, int64_t q, uint64_t* lists) {
+  const int lane = threadIdx.x & 31;
   const uint64_t* c = p.cand + static_cast<size_t>(q) * p.num_sc * KL;
   const int total = p.num_sc * KL;
   uint64_t sel = kEmptyKey;
@@ -160,7 +187,6 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
     }
     sel = lane < KL ? key : kEmptyKey;
   } else {
-    uint64_t* lists = merge_smem + warp * 32 * KL;
     // 1. Each lane keeps the KL best keys of a strided share of the candidates.
     uint64_t L[KL];
 #pragma unroll
@@ -187,31 +213,11 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
   // 3. Exact distance of each survivor.
   const float* x = p.queries + q * p.dim;
   const float xn = p.xn[q];
-  if (p.labels_only && p.k_eff == 1 && p.neighbors && p.allow == nullptr &&
-      p.metric == kMetricL2) {
-    // The approximate ranking values v = |y|^2 - 2 x.y differ from the exact ones by at most
-    // ~1e-6 (|x| |y| + |v|) (split fp16 products, fp32 sums); with a 10x wider margin, a best
-    // candidate that beats the second by more than it is the exact argmin, ties included.
+  if (use_assign_shortcut(p)) {
     const uint64_t k0 = __shfl_sync(kFull, sel, 0), k1 = __shfl_sync(kFull, sel, 1);
-    if (k0 != kEmptyKey) {
-      const float v0 = keys::key_value(k0);
-      const float v1 = k1 == kEmptyKey ? __int_as_float(0x7f800000) : keys::key_value(k1);
-      const float yn0 = p.norm_sorted[p.inv_perm[keys::key_id(k0)]];
-      const float yn1 = k1 == kEmptyKey ? 0.f : p.norm_sorted[p.inv_perm[keys::key_id(k1)]];
-      const float fin = __int_as_float(0x7f800000);
-      const bool finite = fabsf(v0) < fin && fabsf(xn) < fin && fabsf(yn0) < fin &&
-                          fabsf(yn1) < fin && !(v1 != v1);
-      const float margin =
-          1e-5f * (fabsf(v0) + (k1 == kEmptyKey ? 0.f : fabsf(v1)) + xn + yn0 + yn1 +
-                   2.f * sqrtf(xn * yn0) + 2.f * sqrtf(xn * yn1)) + 1e-30f;
-      if (finite && v1 - v0 > margin) {
-        if (lane == 0) {
-          p.neighbors[q] = p.row_offset + static_cast<int64_t>(keys::key_id(k0));
-          p.distances[q] = __fadd_rn(xn, v0);
-        }
-        return;
-      }
-    }
+    bool done = false;
+    if (lane == 0) done = assign_shortcut(p, q, xn, k0, k1);
+    if (__shfl_sync(kFull, done, 0)) return;
   }
   float rank = __int_as_float(0x7fffffff);
   uint64_t key = kEmptyKey;
@@ -252,6 +258,51 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
       p.shard_rank[o] = rank;
       p.shard_gid[o] = empty ? INT64_MAX : gid;
     }
+  }
+}
+
+template <int KL>
+__global__ void __launch_bounds__(kMergeWarps * 32)
+    merge_rerank_kernel(const MergeParams p) {
+  extern __shared__ uint64_t merge_smem[];
+  const int warp = threadIdx.x >> 5;
+  const int64_t q = static_cast<int64_t>(blockIdx.x) * kMergeWarps + warp;
+  if (q >= p.nq) return;
+  merge_query<KL>(p, q, merge_smem + warp * 32 * KL);
+}
+
+// k-means assignment (use_assign_shortcut, at most kAssignMaxCand candidates per point): one
+// thread per point finds its two best candidate keys and takes the shortcut; the points where it
+// does not apply (near-ties) are merged and re-ranked exactly by the whole warp, one at a time.
+constexpr int kAssignMaxCand = 64;
+
+template <int KL>
+__global__ void __launch_bounds__(kMergeWarps * 32)
+    assign_kernel(const MergeParams p) {
+  extern __shared__ uint64_t merge_smem[];
+  const int warp = threadIdx.x >> 5;
+  const int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  bool slow = false;
+  if (q < p.nq) {
+    const int total = p.num_sc * KL;
+    const uint64_t* c = p.cand + static_cast<size_t>(q) * total;
+    uint64_t k0 = kEmptyKey, k1 = kEmptyKey;
+    for (int e = 0; e < total; ++e) {
+      const uint64_t key = c[e];
+      if (key < k0) {
+        k1 = k0;
+        k0 = key;
+      } else if (key < k1) {
+        k1 = key;
+      }
+    }
+    slow = !assign_shortcut(p, q, p.xn[q], k0, k1);
+  }
+  uint32_t pending = __ballot_sync(kFull, slow);
+  while (pending) {
+    const int src = __ffs(pending) - 1;
+    pending &= pending - 1;
+    merge_query<KL>(p, __shfl_sync(kFull, q, src), merge_smem + warp * 32 * KL);
   }
 }
 
@@ -424,13 +475,15 @@ __global__ void __launch_bounds__(256) select_rerank_kernel(const SelectParams s
 template <int KL>
 cudaError_t launch_kl(const MergeParams& p, cudaStream_t stream) {
   const size_t smem = static_cast<size_t>(kMergeWarps) * 32 * KL * sizeof(uint64_t);
-  auto kern = merge_rerank_kernel<KL>;
+  const bool assign = use_assign_shortcut(p) && p.num_sc * KL <= kAssignMaxCand;
+  auto kern = assign ? assign_kernel<KL> : merge_rerank_kernel<KL>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
   }
-  const int64_t blocks = (p.nq + kMergeWarps - 1) / kMergeWarps;
+  const int64_t per_block = assign ? kMergeWarps * 32 : kMergeWarps;  // points or queries
+  const int64_t blocks = (p.nq + per_block - 1) / per_block;
   kern<<<static_cast<unsigned>(blocks), kMergeWarps * 32, smem, stream>>>(p);
   return cudaGetLastError();
 }

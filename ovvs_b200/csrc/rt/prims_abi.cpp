@@ -99,6 +99,7 @@ ovvsStatus gemm_impl(ovvsResources_t res, const float* a, const float* b, float*
     // no device kernel takes the type (mixer.cpp:85-90).
     const int round = compute == OVVS_DTYPE_F16 ? ovvs::prim::kRoundF16 : ovvs::prim::kRoundNone;
     DeviceBuffer da, db, dc;
+    r.mark(0);
     OVVS_TRY(upload(db, b, static_cast<size_t>(k * n) * sizeof(float), r.stream));
     const int64_t rb = std::min(m, block_rows(std::max(n, k), 2 * sizeof(float)));
     OVVS_TRY_CUDA(da.reserve(static_cast<size_t>(rb * k) * sizeof(float) + 16));
@@ -107,11 +108,15 @@ ovvsStatus gemm_impl(ovvsResources_t res, const float* a, const float* b, float*
       const int64_t rows = std::min(rb, m - i0);
       OVVS_TRY_CUDA(cudaMemcpyAsync(da.get(), a + i0 * k, static_cast<size_t>(rows * k) * sizeof(float),
                                     cudaMemcpyHostToDevice, r.stream));
+      if (i0 == 0) r.mark(1);
       OVVS_TRY_CUDA(ovvs::prim::launch_gemm_seq(da.as<float>(), db.as<float>(), dc.as<float>(),
                                                 rows, n, k, trans_b != 0, round, r.stream));
+      if (i0 == 0) r.mark(2);
       OVVS_TRY_CUDA(cudaMemcpyAsync(c + i0 * n, dc.get(), static_cast<size_t>(rows * n) * sizeof(float),
                                     cudaMemcpyDeviceToHost, r.stream));
     }
+    r.mark(3);
+    r.mark(4);
     OVVS_TRY(r.finish());
     r.last_device = OVVS_DEVICE_GPU;
     r.last_compute_dtype = round == ovvs::prim::kRoundF16 ? OVVS_DTYPE_F16 : OVVS_DTYPE_F32;
@@ -205,6 +210,7 @@ ovvsStatus ovvsPairwiseDistance(ovvsResources_t res, ovvsMetric metric, const fl
   return guarded(r, [&]() -> ovvsStatus {
     if (too_big(nx, dim) || too_big(ny, dim) || too_big(nx, ny)) return OVVS_STATUS_SHAPE_MISMATCH;
     DeviceBuffer dx, dy, dyn, dxn, dout;
+    r.mark(0);
     OVVS_TRY(upload(dy, y, static_cast<size_t>(ny * dim) * sizeof(float), r.stream));
     OVVS_TRY_CUDA(dyn.reserve(static_cast<size_t>(ny) * sizeof(float) + 16));
     OVVS_TRY_CUDA(ovvs::prim::launch_row_norms_seq(dy.as<float>(), ny, dim, dyn.as<float>(),
@@ -218,12 +224,16 @@ ovvsStatus ovvsPairwiseDistance(ovvsResources_t res, ovvsMetric metric, const fl
       OVVS_TRY_CUDA(cudaMemcpyAsync(dx.get(), x + i0 * dim,
                                     static_cast<size_t>(rows * dim) * sizeof(float),
                                     cudaMemcpyHostToDevice, r.stream));
+      if (i0 == 0) r.mark(1);
       OVVS_TRY(pairwise_block(r, metric, dx.as<float>(), rows, dy.as<float>(), ny, dim,
                               dyn.as<float>(), metric_arg, dxn.as<float>(), dout.as<float>()));
+      if (i0 == 0) r.mark(2);
       OVVS_TRY_CUDA(cudaMemcpyAsync(out + i0 * ny, dout.get(),
                                     static_cast<size_t>(rows * ny) * sizeof(float),
                                     cudaMemcpyDeviceToHost, r.stream));
     }
+    r.mark(3);
+    r.mark(4);
     OVVS_TRY(r.finish());
     r.last_device = OVVS_DEVICE_GPU;
     return OVVS_STATUS_SUCCESS;
