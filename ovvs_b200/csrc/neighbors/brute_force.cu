@@ -278,9 +278,9 @@ int launch_grid(const prim::FusedParams& p, int num_sms) {
 // Sharded list-mode searches: *own = this rank's bound array in the peer window and
 // p.peer_bound = the other ranks' arrays, so the fused kernel shares each query's bound across
 // ranks. The window is created (and grown) here, collectively: every rank of a sharded search
-// reaches this point with the same q_pad. *own stays null when the window is unavailable or
-// switched off with OVVS_PEER_BOUNDS=0 (which must then be set on every rank); the search then
-// keeps its bound on its own rank.
+// reaches this point with the same q_pad. *own stays null when the window is unavailable (every
+// rank then agrees) or switched off with OVVS_PEER_BOUNDS=0 (which must then be set on every
+// rank); the search then keeps its bound on its own rank.
 ovvsStatus peer_bound_arrays(rt::Resources& r, int64_t q_pad, uint64_t** own,
                              prim::FusedParams& p) {
   *own = nullptr;
@@ -296,8 +296,10 @@ ovvsStatus peer_bound_arrays(rt::Resources& r, int64_t q_pad, uint64_t** own,
     if (r.bound_win.ready()) OVVS_TRY(r.finish());
     const uint64_t tag =
         r.comm_tag ^ (0x9E3779B97F4A7C15ull * static_cast<uint64_t>(++r.window_seq));
-    const ovvsStatus st =
-        r.bound_win.create(r, std::max(need, size_t(1) << 20), tag, r.nccl_timeout_ms);
+    // descriptor exchange bounded by 10 s (or the NCCL deadline if shorter): where the ranks
+    // cannot reach one another's sockets, the search goes on with local bounds after it
+    const ovvsStatus st = r.bound_win.create(r, std::max(need, size_t(1) << 20), tag,
+                                             std::min<int64_t>(r.nccl_timeout_ms, 10000));
     if (st == OVVS_STATUS_UNSUPPORTED) {
       r.peer_bounds = -1;
       return OVVS_STATUS_SUCCESS;

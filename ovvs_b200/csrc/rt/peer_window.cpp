@@ -157,8 +157,9 @@ ovvsStatus PeerWindow::create(Resources& r, size_t bytes, uint64_t tag, int64_t 
   }
   (void)cudaGetLastError();
   // 3. All ranks mapped every buffer, or none uses the window; every rank returns the same
-  // status: ERROR when some rank's exchange failed (a peer did not take part), UNSUPPORTED when
-  // the exchange worked but some mapping did not (no peer access between the devices).
+  // status. This all-reduce completing shows every rank is alive, so a failed exchange (sockets
+  // not reachable between the ranks, e.g. separate network namespaces) or mapping (no peer
+  // access between the devices) means the window is unavailable here: UNSUPPORTED.
   int64_t votes2 = (ok ? 1 : 0) + (exchanged ? world + 1 : 0);
   st = allreduce_i64_sum(r, &votes2);
   if (st != OVVS_STATUS_SUCCESS) {
@@ -168,7 +169,7 @@ ovvsStatus PeerWindow::create(Resources& r, size_t bytes, uint64_t tag, int64_t 
   const int64_t n_exchanged = votes2 / (world + 1), n_mapped = votes2 % (world + 1);
   if (n_exchanged != world || n_mapped != world) {
     reset();
-    return n_exchanged != world ? OVVS_STATUS_ERROR : OVVS_STATUS_UNSUPPORTED;
+    return OVVS_STATUS_UNSUPPORTED;
   }
   ptr_.resize(static_cast<size_t>(world));
   for (int p = 0; p < world; ++p)

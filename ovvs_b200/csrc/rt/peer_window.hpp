@@ -34,9 +34,10 @@ class PeerWindow {
   // Collective over r's ranks (every rank calls it with the same `bytes`, in the same order
   // relative to its other windows): allocates this rank's buffer of at least `bytes` and maps
   // every peer's. `tag` identifies the exchange on the host (derived from the communicator's
-  // unique id and a per-Resources sequence number). Returns SUCCESS, or UNSUPPORTED when the
-  // device or driver cannot share memory this way (nothing is left allocated), or ERROR when
-  // a peer did not take part before the deadline.
+  // unique id and a per-Resources sequence number); `timeout_ms` bounds the descriptor exchange.
+  // Returns SUCCESS; UNSUPPORTED (on every rank alike, nothing left allocated) when some rank
+  // cannot allocate, export, exchange or map; or the error of the communicator's all-reduce
+  // when a rank is gone.
   ovvsStatus create(Resources& r, size_t bytes, uint64_t tag, int64_t timeout_ms);
   void reset();
   // Forgets the mappings without unmapping them (they go with the process): for a Resources
