@@ -1005,10 +1005,14 @@ def run_ivf(args, cfg):
     cand_mean = float(sizes[probes].sum(1).mean())
     macs = nq * cand_mean * dim
     sm_mhz = clk["sm_mhz"] or 1965.0
-    # FP32 lanes per SM x SMs x clock: one separately rounded multiply and one add per MAC
+    # L2 without a bitset and k <= 10 scans on the tensor cores (the fused kernel over (list,
+    # 256 probing pairs) items); the other cases on the CUDA cores, whose peak is the FP32 lanes
+    # per SM x SMs x clock (one separately rounded multiply and one add per MAC)
+    tensor = cfg["metric"] in ("l2", "l2_sqrt") and k <= 10
     fp32_gops = 128 * torch.cuda.get_device_properties(dev).multi_processor_count * sm_mhz / 1e3
     achieved = 2 * macs / (scan_ms / 1e3) / 1e12
-    peak = fp32_gops / 1e3
+    peaks, _ = _peaks()
+    peak = float(peaks.get("bf16_tflops", 1590.0)) if tensor else fp32_gops / 1e3
     ix.close()
     res.close()
     line = None
@@ -1029,14 +1033,25 @@ def run_ivf(args, cfg):
             "e2e": {"value": world * nq / (e2e_ms / 1e3), "unit": "queries/s",
                     "h2d_bytes_per_step": nq * dim * 4, "d2h_bytes_per_step": nq * k * 12},
             # row norms, coarse GEMM + L2 epilogue + probe selection, probe offsets, pair
-            # grouping, item counts, list scan, merge/emit (the two CUB scans are library code)
-            "gpu_launches": 9 * args.steps,
-            "roofline": {"bound": "fp32", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": None, "kernel": "list_scan_kernel",
-                         "flops_per_launch": 2 * macs,
-                         "note": "exact sequential fp32 scores (separate multiply and add) on the "
-                                 "CUDA cores; peak = 128 FP32 lanes x SMs x median SM clock, one "
-                                 "instruction per flop"},
+            # grouping, item counts, list scan, merge/emit; the tensor-core scan adds slot counts,
+            # slot fill, query prep, slot gather and the re-score and replaces the scan by the
+            # fused kernel (the CUB scans are library code)
+            "gpu_launches": (14 if tensor else 9) * args.steps,
+            "roofline": ({"bound": "tensor", "achieved": achieved, "peak": peak,
+                          "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                          "kernel": "knn_fused_kernel (list items) + exact re-score",
+                          "flops_per_launch": 2 * macs,
+                          "note": "algorithmic 2*D*(rows of the probed lists) per query; fp32 "
+                                  "rows and queries run as three fp16 MMA passes; phase [1] = "
+                                  "slot layout, fused kernel and re-score; peak = measured "
+                                  "bf16 dense burst"}
+                         if tensor else
+                         {"bound": "fp32", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                          "frac": achieved / peak, "traffic": None, "kernel": "list_scan_kernel",
+                          "flops_per_launch": 2 * macs,
+                          "note": "exact sequential fp32 scores (separate multiply and add) on "
+                                  "the CUDA cores; peak = 128 FP32 lanes x SMs x median SM clock, "
+                                  "one instruction per flop"}),
             "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"],
                        "reasons": clk["reasons"]},
         }

@@ -187,6 +187,86 @@ ovvsStatus build_from_device(rt::Resources& r, BruteIndex& ix, const void* d_dat
   return OVVS_STATUS_SUCCESS;
 }
 
+namespace {
+
+__global__ void mask_padding_aux_kernel(float* __restrict__ aux, const int64_t* __restrict__ real,
+                                        int64_t n) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n && real[i] < 0) aux[i] = __int_as_float(0x7f800000);
+}
+
+}  // namespace
+
+ovvsStatus build_in_order(rt::Resources& r, BruteIndex& ix, const float* d_rows, int64_t n,
+                          int64_t dim, int metric_raw, const int64_t* d_real) {
+  if (n >= static_cast<int64_t>(keys::kEmptyId) || dim > 4096) return OVVS_STATUS_SHAPE_MISMATCH;
+  ix.device = r.device;
+  ix.sharded = false;
+  ix.n = n;
+  ix.n_total = n;
+  ix.row_offset = 0;
+  ix.dim = dim;
+  ix.metric_raw = metric_raw;
+  ix.metric = prim::normalize_metric(metric_raw);
+  ix.dtype = kDTypeF32;
+  ix.dp = static_cast<int>((dim + 15) / 16 * 16);
+  if (!plan_chunks(ix.dp, prim::kMaxChunks, &ix.nchunk, ix.chunk_x, ix.chunk_w))
+    return OVVS_STATUS_UNSUPPORTED;
+  if (prim::rank_kind_of(ix.metric) != prim::kRankAffine) return OVVS_STATUS_UNSUPPORTED;
+  ix.b_parts = 2;
+  ix.n_pad = (n + kTileN - 1) / kTileN * kTileN;
+  ix.num_tiles = static_cast<int>(ix.n_pad / kTileN);
+  cudaStream_t s = r.stream;
+  rt::DeviceBuffer norm, key, perm, absmax;
+  OVVS_TRY_CUDA(norm.reserve(n * sizeof(float)));
+  OVVS_TRY_CUDA(key.reserve(n * sizeof(float)));
+  OVVS_TRY_CUDA(perm.reserve(n * sizeof(uint32_t)));
+  OVVS_TRY_CUDA(absmax.reserve(sizeof(unsigned int)));
+  OVVS_TRY_CUDA(cudaMemsetAsync(absmax.get(), 0, sizeof(unsigned int), s));
+  prim::launch_row_stats(d_rows, kDTypeF32, n, static_cast<int>(dim), ix.metric, norm.as<float>(),
+                         key.as<float>(), absmax.as<unsigned int>(), s);
+  OVVS_TRY_CUDA(cudaGetLastError());
+  std::vector<uint32_t> iota(static_cast<size_t>(n));
+  for (int64_t i = 0; i < n; ++i) iota[static_cast<size_t>(i)] = static_cast<uint32_t>(i);
+  OVVS_TRY_CUDA(cudaMemcpyAsync(perm.get(), iota.data(), n * sizeof(uint32_t),
+                                cudaMemcpyHostToDevice, s));
+  unsigned int bits = 0;
+  OVVS_TRY_CUDA(cudaMemcpyAsync(&bits, absmax.get(), sizeof(bits), cudaMemcpyDeviceToHost, s));
+  OVVS_TRY_CUDA(cudaStreamSynchronize(s));  // iota and bits
+  float mx;
+  std::memcpy(&mx, &bits, sizeof(mx));
+  ix.e_db = mx > 0.f ? std::min(14 - std::ilogb(mx), 127) : 0;
+  const int stride = ix.b_parts * ix.dp;
+  OVVS_TRY_CUDA(ix.rows16.reserve(static_cast<size_t>(ix.n_pad) * stride * 2));
+  ix.exact32.release();
+  OVVS_TRY_CUDA(ix.aux.reserve(ix.n_pad * sizeof(float)));
+  OVVS_TRY_CUDA(ix.norm_sorted.reserve(ix.n_pad * sizeof(float)));
+  OVVS_TRY_CUDA(ix.row_id.reserve(ix.n_pad * sizeof(uint32_t)));
+  OVVS_TRY_CUDA(ix.inv_perm.reserve(n * sizeof(uint32_t)));
+  OVVS_TRY_CUDA(ix.tile_aux.reserve((ix.num_tiles + prim::group_count(ix.num_tiles)) * sizeof(float2)));
+  prim::launch_scatter_rows(d_rows, kDTypeF32, n, ix.n_pad, static_cast<int>(dim), ix.dp,
+                            ix.b_parts, ix.metric, ix.e_db, perm.as<uint32_t>(), norm.as<float>(),
+                            key.as<float>(), ix.rows16.as<__half>(), nullptr, ix.aux.as<float>(),
+                            ix.norm_sorted.as<float>(), ix.row_id.as<uint32_t>(),
+                            ix.inv_perm.as<uint32_t>(), s);
+  OVVS_TRY_CUDA(cudaGetLastError());
+  if (d_real && n > 0) {
+    mask_padding_aux_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(
+        ix.aux.as<float>(), d_real, n);
+    OVVS_TRY_CUDA(cudaGetLastError());
+  }
+  prim::launch_tile_bounds(ix.aux.as<float>(), n, ix.num_tiles, ix.tile_aux.as<float2>(), s);
+  OVVS_TRY_CUDA(cudaGetLastError());
+  const uint64_t cols = static_cast<uint64_t>(stride);
+  if (!rt::encode_f16_2d(&ix.b64, ix.rows16.get(), cols, ix.n_pad, 64, prim::kHalfN) ||
+      !rt::encode_f16_2d(&ix.b32, ix.rows16.get(), cols, ix.n_pad, 32, prim::kHalfN) ||
+      !rt::encode_f16_2d(&ix.b16, ix.rows16.get(), cols, ix.n_pad, 16, prim::kHalfN)) {
+    return OVVS_STATUS_ERROR;
+  }
+  OVVS_TRY_CUDA(cudaStreamSynchronize(s));
+  return OVVS_STATUS_SUCCESS;
+}
+
 ovvsStatus build_from_host(rt::Resources& r, BruteIndex& ix, const void* data, int dtype,
                            int64_t n, int64_t dim, int metric_raw, int64_t row_offset,
                            bool sharded) {

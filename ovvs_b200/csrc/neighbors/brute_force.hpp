@@ -54,6 +54,13 @@ struct BruteIndex {
 ovvsStatus build_from_device(rt::Resources& r, BruteIndex& ix, const void* d_data, int dtype,
                              int64_t n, int64_t dim, int metric_raw, int64_t row_offset);
 
+// Index over fp32 device rows kept in their given order (positions = row numbers, no norm sort,
+// no exact copy), for callers that address rows by position (the IVF-Flat list scan). Rows with
+// d_real[i] < 0 are padding: their aux is +inf, so the exact-value filter never selects them.
+// L2 family only (UNSUPPORTED otherwise).
+ovvsStatus build_in_order(rt::Resources& r, BruteIndex& ix, const float* d_rows, int64_t n,
+                          int64_t dim, int metric_raw, const int64_t* d_real);
+
 // Builds from host rows (copied to the device). `sharded`: the rows are this rank's shard of a
 // dataset spread over r's ranks (collective: every rank calls it).
 ovvsStatus build_from_host(rt::Resources& r, BruteIndex& ix, const void* data, int dtype,

@@ -11,6 +11,7 @@
 #include "../cluster/kmeans.hpp"
 #include "../prim/dense.cuh"
 #include "../prim/ivf_scan.cuh"
+#include "../prim/prep.cuh"
 
 namespace ovvs {
 namespace ivf {
@@ -24,7 +25,50 @@ size_t bytes_of(int64_t count, size_t elem) {
   return static_cast<size_t>(count > 0 ? count : 1) * elem;
 }
 
-// Device copies of the host list layout, and the list-ordered rows gathered from d_x.
+bool tc_metric(int metric) {
+  return metric == OVVS_METRIC_L2_EXPANDED || metric == OVVS_METRIC_L2_SQRT_EXPANDED;
+}
+
+// The tensor-core scan's operand: every list padded to whole 256-row tiles, in list order.
+ovvsStatus assemble_tc(rt::Resources& r, IvfFlatIndex& ix) {
+  ix.tc_ready = false;
+  const int64_t rows = ix.list_off.back();
+  if (!tc_metric(ix.metric) || rows <= 0 || ix.nlist <= 0) return OVVS_STATUS_SUCCESS;
+  cudaStream_t s = r.stream;
+  std::vector<int64_t> lpos(static_cast<size_t>(ix.nlist) + 1, 0);
+  std::vector<int2> tiles(static_cast<size_t>(ix.nlist));
+  for (int c = 0; c < ix.nlist; ++c) {
+    const int64_t size = ix.list_off[c + 1] - ix.list_off[c];
+    lpos[c + 1] = lpos[c] + (size + 255) / 256 * 256;
+    tiles[c] = make_int2(static_cast<int>(lpos[c] / 256), static_cast<int>(lpos[c + 1] / 256));
+  }
+  const int64_t n_tc = lpos.back();
+  std::vector<int64_t> pos_row(static_cast<size_t>(n_tc), -1);
+  for (int c = 0; c < ix.nlist; ++c)
+    for (int64_t i = 0; i < ix.list_off[c + 1] - ix.list_off[c]; ++i)
+      pos_row[static_cast<size_t>(lpos[c] + i)] = ix.list_off[c] + i;
+  OVVS_TRY_CUDA(ix.d_pos_row.reserve(bytes_of(n_tc, sizeof(int64_t))));
+  OVVS_TRY_CUDA(ix.d_list_tiles.reserve(bytes_of(ix.nlist, sizeof(int2))));
+  OVVS_TRY_CUDA(cudaMemcpyAsync(ix.d_pos_row.get(), pos_row.data(), n_tc * sizeof(int64_t),
+                                cudaMemcpyHostToDevice, s));
+  OVVS_TRY_CUDA(cudaMemcpyAsync(ix.d_list_tiles.get(), tiles.data(), ix.nlist * sizeof(int2),
+                                cudaMemcpyHostToDevice, s));
+  rt::DeviceBuffer padded, pnorm;
+  OVVS_TRY_CUDA(padded.reserve(bytes_of(n_tc * ix.dim, sizeof(float))));
+  OVVS_TRY_CUDA(pnorm.reserve(bytes_of(n_tc, sizeof(float))));
+  OVVS_TRY_CUDA(prim::launch_ivf_gather_rows(ix.d_rows.as<float>(), rows, static_cast<int>(ix.dim),
+                                             ix.d_pos_row.as<int64_t>(), n_tc,
+                                             padded.as<float>(), pnorm.as<float>(), s));
+  const ovvsStatus st = nb::build_in_order(r, ix.tc, padded.as<float>(), n_tc, ix.dim, ix.metric,
+                                           ix.d_pos_row.as<int64_t>());
+  if (st == OVVS_STATUS_UNSUPPORTED) return OVVS_STATUS_SUCCESS;  // the CUDA-core scan serves
+  OVVS_TRY(st);
+  ix.tc_ready = true;
+  return r.finish();
+}
+
+// Device copies of the host list layout, the list-ordered rows gathered from d_x and the
+// tensor-core scan's operand.
 ovvsStatus assemble(rt::Resources& r, IvfFlatIndex& ix) {
   cudaStream_t s = r.stream;
   const int64_t rows = ix.list_off.back();
@@ -41,7 +85,8 @@ ovvsStatus assemble(rt::Resources& r, IvfFlatIndex& ix) {
                                                ix.d_ids.as<int64_t>(), rows, ix.d_rows.as<float>(),
                                                ix.d_rnorm.as<float>(), s));
   }
-  return r.finish();
+  OVVS_TRY(r.finish());
+  return assemble_tc(r, ix);
 }
 
 // Device centroids, their norms (nrm2sq, sequential) and the assignment index.
@@ -74,6 +119,104 @@ ovvsStatus assign(rt::Resources& r, IvfFlatIndex& ix, const float* d_rows, int64
   OVVS_TRY_CUDA(cudaMemcpyAsync(labels.data(), lab.get(), n * sizeof(int64_t),
                                 cudaMemcpyDeviceToHost, r.stream));
   return r.finish();
+}
+
+// The list scan of one query block on the tensor cores (ivf_flat.hpp: L2 metrics, no bitset,
+// k <= 10): slots for the block's (query, probe) pairs grouped by list, one fused-kernel item per
+// (list, 256 slots) over the list's tiles with the exact-value filter, then every pair's
+// candidates re-scored exactly into p.cand (select-mode lists of k for launch_ivf_emit).
+ovvsStatus scan_tc(rt::Resources& r, const IvfFlatIndex& ix, prim::IvfScanParams& p, int64_t k,
+                   const int* lcnt, const int* loff, const int* pairs, void* tmp,
+                   size_t tmp_bytes) {
+  cudaStream_t s = r.stream;
+  const int nlist = ix.nlist;
+  const nb::BruteIndex& tc = ix.tc;
+  const int kl = nb::list_size_for(k);
+  const int2* tiles = ix.d_list_tiles.as<int2>();
+  const int64_t npairs = p.nq * p.nprobe;
+  // 1. slots and items per list, and their totals on the host
+  int* cnt = nullptr;
+  OVVS_TRY(r.scratch(rt::kWsIvfTcCounts, static_cast<size_t>(4) * (nlist + 1), &cnt));
+  int* slot_cnt = cnt;
+  int* item_cnt = cnt + (nlist + 1);
+  int* slot_off = cnt + 2 * (nlist + 1);
+  int* item_off = cnt + 3 * (nlist + 1);
+  OVVS_TRY_CUDA(prim::launch_ivf_tc_counts(lcnt, tiles, nlist, slot_cnt, item_cnt, s));
+  size_t tb = tmp_bytes;
+  OVVS_TRY_CUDA(cub::DeviceScan::ExclusiveSum(tmp, tb, slot_cnt, slot_off, nlist + 1, s));
+  tb = tmp_bytes;
+  OVVS_TRY_CUDA(cub::DeviceScan::ExclusiveSum(tmp, tb, item_cnt, item_off, nlist + 1, s));
+  int totals[2] = {0, 0};
+  OVVS_TRY_CUDA(cudaMemcpyAsync(&totals[0], slot_off + nlist, sizeof(int), cudaMemcpyDeviceToHost, s));
+  OVVS_TRY_CUDA(cudaMemcpyAsync(&totals[1], item_off + nlist, sizeof(int), cudaMemcpyDeviceToHost, s));
+  OVVS_TRY_CUDA(cudaStreamSynchronize(s));
+  const int64_t slots = totals[0];
+  const int items = totals[1];
+  // 2. slot <-> pair maps and the item table
+  int *slot_pair = nullptr, *pair_slot = nullptr;
+  int4* item_tab = nullptr;
+  OVVS_TRY(r.scratch(rt::kWsIvfTcSlotPair, static_cast<size_t>(std::max<int64_t>(slots, 1)),
+                     &slot_pair));
+  OVVS_TRY(r.scratch(rt::kWsIvfTcPairSlot, static_cast<size_t>(npairs), &pair_slot));
+  OVVS_TRY(r.scratch(rt::kWsIvfTcItems, static_cast<size_t>(std::max(items, 1)), &item_tab));
+  OVVS_TRY_CUDA(cudaMemsetAsync(pair_slot, 0xFF, npairs * sizeof(int), s));
+  OVVS_TRY_CUDA(prim::launch_ivf_tc_fill(lcnt, loff, pairs, slot_off, item_off, tiles, nlist,
+                                         slot_pair, pair_slot, item_tab, s));
+  uint64_t* cand = nullptr;
+  OVVS_TRY(r.scratch(rt::kWsIvfTcCand,
+                     static_cast<size_t>(std::max<int64_t>(slots, 1)) * 2 * kl, &cand));
+  if (items > 0) {
+    // 3. the fused kernel's query operand per slot
+    const int64_t q_pad = prim::pad_queries(p.nq);
+    const int halves = 2 * tc.dp;
+    __half *qa = nullptr, *sa = nullptr;
+    float *qmul = nullptr, *smul = nullptr, *qxn = nullptr;
+    int* flag = nullptr;
+    uint64_t* bound = nullptr;
+    OVVS_TRY(r.scratch(rt::kWsIvfTcQueryA, static_cast<size_t>(q_pad) * halves, &qa));
+    OVVS_TRY(r.scratch(rt::kWsIvfTcSlotA, static_cast<size_t>(slots) * halves, &sa));
+    OVVS_TRY(r.scratch(rt::kWsIvfTcQueryMul, static_cast<size_t>(q_pad), &qmul));
+    OVVS_TRY(r.scratch(rt::kWsIvfTcSlotMul, static_cast<size_t>(slots), &smul));
+    OVVS_TRY(r.scratch(rt::kWsIvfTcQueryNorm, static_cast<size_t>(q_pad), &qxn));
+    OVVS_TRY(r.scratch(rt::kWsIvfTcFlag, 4, &flag));
+    OVVS_TRY(r.scratch(rt::kWsIvfTcBound, static_cast<size_t>(slots), &bound));
+    OVVS_TRY_CUDA(cudaMemsetAsync(flag, 0, sizeof(int), s));
+    prim::launch_query_prep(p.queries, p.nq, q_pad, p.dim, tc.dp, tc.metric, tc.e_db, qa, qmul,
+                            qxn, flag, s);
+    OVVS_TRY_CUDA(cudaGetLastError());
+    OVVS_TRY_CUDA(prim::launch_ivf_tc_gather(qa, qmul, slot_pair, p.nprobe, slots, halves, sa,
+                                             smul, s));
+    // 4. one item per (list, 256 slots) over the list's tiles
+    nb::SearchCtx c;
+    c.q_pad = slots;
+    c.num_qtiles = static_cast<int>(slots / prim::kTileQ);
+    c.a16 = sa;
+    c.q_mul = smul;
+    c.xn = qxn;
+    c.flag = flag;
+    OVVS_TRY(nb::encode_query_maps(c, tc.dp));
+    c.maps.b64 = tc.b64;
+    c.maps.b32 = tc.b32;
+    c.maps.b16 = tc.b16;
+    prim::FusedParams fp;
+    OVVS_TRY(nb::base_params(r, tc, c, slots, &fp));
+    fp.item_tab = item_tab;
+    fp.slot_pair = slot_pair;
+    fp.num_items = items;
+    fp.num_sc = 1;
+    fp.tiles_per_item = 1;
+    fp.exact_filter = 1;
+    OVVS_TRY_CUDA(cudaMemsetAsync(bound, 0xFF, static_cast<size_t>(slots) * sizeof(uint64_t), s));
+    fp.q_bound = bound;
+    fp.k_pub = static_cast<int>(k);
+    fp.out = cand;
+    OVVS_TRY_CUDA(prim::launch_knn_fused(c.maps, fp, kl,
+                                         prim::fused_grid(items, nb::pair_sms(r, fp)), s));
+  }
+  // 5. exact re-score of every pair's candidates
+  p.k_sel = static_cast<int>(k);
+  OVVS_TRY_CUDA(prim::launch_ivf_tc_refine(p, cand, kl, pair_slot, ix.d_pos_row.as<int64_t>(), s));
+  return OVVS_STATUS_SUCCESS;
 }
 
 }  // namespace
@@ -188,6 +331,8 @@ ovvsStatus search_device(rt::Resources& r, const IvfFlatIndex& ix, const float* 
   else
     qb = std::min<int64_t>(qb, std::max<int64_t>(1, (int64_t(1) << 27) / (int64_t(nprobe) * k)));
   const bool coarse_sort = nprobe > prim::kIvfMaxSelect;
+  // the tensor-core scan: L2 metrics, no bitset, k within its 12-entry lists
+  const bool use_tc = ix.tc_ready && d_bitset == nullptr && k <= 10 && !sort_mode;
 
   float *qn = nullptr, *sc = nullptr, *pval = nullptr;
   int64_t* probe = nullptr;
@@ -288,7 +433,12 @@ ovvsStatus search_device(rt::Resources& r, const IvfFlatIndex& ix, const float* 
     if (marks) r.mark(1);  // phase 1 = the list scan (and, for k > 256, the segment sort)
     int64_t* out_n = d_neighbors + q0 * k;
     float* out_d = d_distances + q0 * k;
-    if (!sort_mode) {
+    if (use_tc) {
+      p.cand = ckeys;
+      OVVS_TRY(scan_tc(r, ix, p, k, lcnt, loff, pairs, tmp, tmp_bytes));
+      if (marks) r.mark(2);
+      OVVS_TRY_CUDA(prim::launch_ivf_emit(p, nullptr, k, out_n, out_d, s));
+    } else if (!sort_mode) {
       p.k_sel = static_cast<int>(k);
       p.cand = ckeys;
       OVVS_TRY_CUDA(prim::launch_ivf_scan_select(p, grid, s));

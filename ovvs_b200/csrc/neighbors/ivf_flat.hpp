@@ -9,7 +9,11 @@
 //            ascending row order.
 //   search:  coarse squared-L2 scores of each query against the centroids (sequential fp32 on
 //            CUDA cores, the reference's prim_pairwise arithmetic) and its nprobe nearest lists;
-//            then the list scan of prim/ivf_scan.cu.
+//            then the list scan: for the L2 metrics without a bitset and k <= 10 on the tensor
+//            cores (the fused brute-force kernel over (list, 256 probing pairs) items, then an
+//            exact re-score of each pair's candidates: the reference's results except where a
+//            row ties with a pair's k-th within the approximate scores' error, as for the
+//            brute-force search), otherwise the exact CUDA-core scan of prim/ivf_scan.cu.
 // Device layout: the dataset in original row order (kept for serialisation and extension) and a
 // copy in list order (the scan's operand) with each row's squared norm and original id; the
 // centroids and their norms; list offsets. The lists themselves are mirrored on the host, as in
@@ -38,6 +42,12 @@ struct IvfFlatIndex {
   rt::DeviceBuffer d_rows, d_rnorm, d_ids, d_loff;  // list order
   rt::DeviceBuffer d_cent, d_cnorm;
   nb::BruteIndex cindex;            // the centroids as an L2 brute-force index (assignment)
+  // Tensor-core list scan (L2 family): the list-ordered rows with every list padded to whole
+  // 256-row tiles, as an in-order brute-force index; pos_row[pos] = the list-order row of a
+  // padded position (-1: padding); list_tiles[c] = (first tile, end tile) of list c.
+  nb::BruteIndex tc;
+  rt::DeviceBuffer d_pos_row, d_list_tiles;
+  bool tc_ready = false;
 };
 
 ovvsStatus build(rt::Resources& r, IvfFlatIndex& ix, const float* x, int64_t n, int64_t dim,

@@ -564,6 +564,96 @@ cudaError_t launch_scan(const IvfScanParams& p, int64_t grid, cudaStream_t strea
   }
 }
 
+// ---- tensor-core list scan helpers ---------------------------------------------------------
+constexpr int kTcSlots = 256;  // slots per pair tile of the fused kernel
+
+__global__ void tc_counts_kernel(const int* __restrict__ list_q_count,
+                                 const int2* __restrict__ list_tiles, int nlist,
+                                 int* __restrict__ slot_count, int* __restrict__ item_count) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c > nlist) return;
+  // an empty list gets no slots (its pairs have no candidates)
+  const int cnt = c < nlist && list_tiles[c].y > list_tiles[c].x ? list_q_count[c] : 0;
+  const int padded = (cnt + kTcSlots - 1) / kTcSlots * kTcSlots;
+  slot_count[c] = padded;
+  item_count[c] = padded / kTcSlots;
+}
+
+// One block per list.
+__global__ void tc_fill_kernel(const int* __restrict__ list_q_count,
+                               const int* __restrict__ list_q_off, const int* __restrict__ pair_of,
+                               const int* __restrict__ slot_off, const int* __restrict__ item_off,
+                               const int2* __restrict__ list_tiles, int* __restrict__ slot_pair,
+                               int* __restrict__ pair_slot, int4* __restrict__ item_tab) {
+  const int c = blockIdx.x;
+  const int cnt = list_q_count[c];
+  const int s0 = slot_off[c], ns = slot_off[c + 1] - s0;
+  for (int i = threadIdx.x; i < ns; i += blockDim.x) {
+    const int pair = i < cnt ? pair_of[list_q_off[c] + i] : -1;
+    slot_pair[s0 + i] = pair;
+    if (pair >= 0) pair_slot[pair] = s0 + i;
+  }
+  const int i0 = item_off[c], ni = item_off[c + 1] - i0;
+  const int2 tiles = list_tiles[c];
+  for (int j = threadIdx.x; j < ni; j += blockDim.x)
+    item_tab[i0 + j] = make_int4(s0 / kTcSlots + j, tiles.x, tiles.y, 0);
+}
+
+// One warp per slot; rows of row_halves fp16 values copied as 16-byte words.
+__global__ void tc_gather_kernel(const uint4* __restrict__ a16_query,
+                                 const float* __restrict__ q_mul_query,
+                                 const int* __restrict__ slot_pair, int nprobe, int64_t slots,
+                                 int words, uint4* __restrict__ a16_slot,
+                                 float* __restrict__ q_mul_slot) {
+  const int lane = threadIdx.x & 31;
+  const int64_t s = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (s >= slots) return;
+  const int pair = slot_pair[s];
+  const int64_t q = pair >= 0 ? pair / nprobe : 0;
+  for (int w = lane; w < words; w += 32)
+    a16_slot[s * words + w] = pair >= 0 ? a16_query[q * words + w] : make_uint4(0, 0, 0, 0);
+  if (lane == 0) q_mul_slot[s] = pair >= 0 ? q_mul_query[q] : -1.f;
+}
+
+// One warp per (query, probe) pair; kl <= 16, so its 2 * kl candidates fit one per lane.
+__global__ void tc_refine_kernel(const __grid_constant__ IvfScanParams p,
+                                 const uint64_t* __restrict__ tc_cand, int kl,
+                                 const int* __restrict__ pair_slot,
+                                 const int64_t* __restrict__ pos_row) {
+  const int lane = threadIdx.x & 31;
+  const int64_t pair = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (pair >= p.nq * p.nprobe) return;
+  const int64_t q = pair / p.nprobe;
+  const int pr = static_cast<int>(pair % p.nprobe);
+  const int slot = pair_slot[pair];
+  uint64_t key = keys::kEmptyKey;
+  if (slot >= 0 && lane < 2 * kl) {
+    const uint64_t c = tc_cand[static_cast<int64_t>(slot) * 2 * kl + lane];
+    // a list shorter than kl may hold padding positions (ranking value +inf): skipped
+    const int64_t g = c != keys::kEmptyKey ? pos_row[keys::key_id(c)] : -1;
+    if (g >= 0) {
+      const int64_t list = p.probe[pair];
+      const uint32_t concat =
+          p.cum[q * (p.nprobe + 1) + pr] + static_cast<uint32_t>(g - p.list_off[list]);
+      const float v = exact_score(p.metric, p.queries + q * p.dim, p.q_norm[q],
+                                  p.rows + g * p.dim, p.row_norm[g], p.dim);
+      key = keys::make_key(v, concat);
+    }
+  }
+  // ascending bitonic sort of the 32 keys; lane r keeps the r-th
+#pragma unroll
+  for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      const uint64_t other = __shfl_xor_sync(0xffffffffu, key, stride);
+      const bool up = (lane & size) == 0;
+      const bool lower = (lane & stride) == 0;
+      key = (lower == up) ? (other < key ? other : key) : (other > key ? other : key);
+    }
+  }
+  if (lane < p.k_sel) p.cand[pair * p.k_sel + lane] = key;
+}
+
 }  // namespace
 
 int64_t ivf_max_items(int64_t nq, int nprobe, int nlist) {
@@ -651,6 +741,46 @@ cudaError_t launch_ivf_seg_bounds(const int64_t* seg_base, const uint32_t* cum, 
   if (nq <= 0) return cudaSuccess;
   seg_bounds_kernel<<<static_cast<unsigned>((nq + 255) / 256), 256, 0, stream>>>(
       seg_base, cum, nq, nprobe, seg_begin, seg_end);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ivf_tc_counts(const int* list_q_count, const int2* list_tiles, int nlist,
+                                 int* slot_count, int* item_count, cudaStream_t stream) {
+  tc_counts_kernel<<<static_cast<unsigned>((nlist + 1 + 255) / 256), 256, 0, stream>>>(
+      list_q_count, list_tiles, nlist, slot_count, item_count);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ivf_tc_fill(const int* list_q_count, const int* list_q_off, const int* pair_of,
+                               const int* slot_off, const int* item_off, const int2* list_tiles,
+                               int nlist, int* slot_pair, int* pair_slot, int4* item_tab,
+                               cudaStream_t stream) {
+  if (nlist <= 0) return cudaSuccess;
+  tc_fill_kernel<<<static_cast<unsigned>(nlist), 256, 0, stream>>>(
+      list_q_count, list_q_off, pair_of, slot_off, item_off, list_tiles, slot_pair, pair_slot,
+      item_tab);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ivf_tc_gather(const void* a16_query, const float* q_mul_query,
+                                 const int* slot_pair, int nprobe, int64_t slots, int row_halves,
+                                 void* a16_slot, float* q_mul_slot, cudaStream_t stream) {
+  if (slots <= 0) return cudaSuccess;
+  if (row_halves % 8 != 0) return cudaErrorInvalidValue;  // whole 16-byte words per row
+  tc_gather_kernel<<<static_cast<unsigned>((slots + 7) / 8), 256, 0, stream>>>(
+      static_cast<const uint4*>(a16_query), q_mul_query, slot_pair, nprobe, slots, row_halves / 8,
+      static_cast<uint4*>(a16_slot), q_mul_slot);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ivf_tc_refine(const IvfScanParams& p, const uint64_t* tc_cand, int kl,
+                                 const int* pair_slot, const int64_t* pos_row,
+                                 cudaStream_t stream) {
+  if (kl < 1 || kl > 16 || p.k_sel < 1 || p.k_sel > 2 * kl) return cudaErrorInvalidValue;
+  const int64_t pairs = p.nq * p.nprobe;
+  if (pairs <= 0) return cudaSuccess;
+  tc_refine_kernel<<<static_cast<unsigned>((pairs + 7) / 8), 256, 0, stream>>>(p, tc_cand, kl,
+                                                                              pair_slot, pos_row);
   return cudaGetLastError();
 }
 

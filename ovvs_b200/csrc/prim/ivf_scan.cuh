@@ -96,6 +96,43 @@ cudaError_t launch_ivf_totals(const uint32_t* cum, int64_t nq, int nprobe, int64
 cudaError_t launch_ivf_seg_bounds(const int64_t* seg_base, const uint32_t* cum, int64_t nq,
                                   int nprobe, int* seg_begin, int* seg_end, cudaStream_t stream);
 
+// ---- tensor-core list scan (L2 family, no bitset, k up to 10) --------------------------------
+// The (query, probe) pairs of each list get "slots": list c's pairs occupy slots
+// [slot_off[c], slot_off[c] + list_q_count[c]) of a range padded to whole 256-slot pair tiles, and
+// the fused brute-force kernel runs one item per (list, pair tile) over the list's database tiles
+// (an item table). Then every pair's two candidate lists are re-scored exactly and written as the
+// select-mode candidate lists that launch_ivf_emit merges.
+
+// slot_count[c] = list_q_count[c] rounded up to 256 (0 for an empty list, whose pairs get no
+// slot), item_count[c] = slot_count[c] / 256 for c < nlist, and both 0 at c = nlist (exclusive
+// scans of nlist + 1 entries give the offsets).
+cudaError_t launch_ivf_tc_counts(const int* list_q_count, const int2* list_tiles, int nlist,
+                                 int* slot_count, int* item_count, cudaStream_t stream);
+
+// slot_pair[s] = q * nprobe + p of slot s (-1 for padding slots), pair_slot[q * nprobe + p] = s
+// (pairs of empty lists keep the caller's -1),
+// and item_tab[i] = (pair tile of the slots, first database tile, end database tile, 0) for the
+// items of every list; list_tiles[c] = (first tile, end tile) of list c in the padded operand.
+cudaError_t launch_ivf_tc_fill(const int* list_q_count, const int* list_q_off, const int* pair_of,
+                               const int* slot_off, const int* item_off, const int2* list_tiles,
+                               int nlist, int* slot_pair, int* pair_slot, int4* item_tab,
+                               cudaStream_t stream);
+
+// The fused kernel's query operand per slot: row s of a16_slot = row (slot_pair[s] / nprobe) of
+// a16_query (zeros for padding slots), row_halves fp16 values each; q_mul_slot likewise (-1 for
+// padding).
+cudaError_t launch_ivf_tc_gather(const void* a16_query, const float* q_mul_query,
+                                 const int* slot_pair, int nprobe, int64_t slots, int row_halves,
+                                 void* a16_slot, float* q_mul_slot, cudaStream_t stream);
+
+// Per pair: its slot's two candidate lists of kl keys (approximate value, padded position) from
+// the fused kernel, re-scored exactly (the scan's arithmetic) and keyed by (score, position in
+// the query's concatenation); the k_sel smallest, ascending, go to p.cand[pair * k_sel ...].
+// pos_row[pos] = the list-order row of a padded position.
+cudaError_t launch_ivf_tc_refine(const IvfScanParams& p, const uint64_t* tc_cand, int kl,
+                                 const int* pair_slot, const int64_t* pos_row,
+                                 cudaStream_t stream);
+
 // Layout kernels: rows[g] = x[ids[g]] (zero row when the id is outside [0, n_x)) and
 // row_norm[g] = nrm2sq(rows[g]), for g < n_rows.
 cudaError_t launch_ivf_gather_rows(const float* x, int64_t n_x, int dim, const int64_t* ids,

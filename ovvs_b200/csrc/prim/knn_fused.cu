@@ -68,8 +68,16 @@ struct Item {
   int qt, sc, t0, t1;
 };
 __device__ __forceinline__ Item item_of(const FusedParams& p, int item, uint32_t rank) {
-  const int num_qpairs = p.num_qtiles >> 1;
   Item it;
+  if (p.item_tab != nullptr) {
+    const int4 e = p.item_tab[item];
+    it.qt = 2 * e.x + static_cast<int>(rank);
+    it.sc = 0;
+    it.t0 = e.y;
+    it.t1 = e.z;
+    return it;
+  }
+  const int num_qpairs = p.num_qtiles >> 1;
   const int qp = item % num_qpairs;
   it.qt = 2 * qp + static_cast<int>(rank);
   it.sc = item / num_qpairs;
@@ -809,7 +817,7 @@ __device__ void run_epilogue(const FusedParams& p, const Smem& s, uint32_t tmem_
     const int64_t q = static_cast<int64_t>(it.qt) * kTileQ + quarter * 32 + lane;
     st.m = p.q_mul[q];
     st.inv_m = 1.0f / st.m;
-    st.real = q < p.nq;
+    st.real = q < p.nq && (p.slot_pair == nullptr || p.slot_pair[q] >= 0);
     st.qi = q;
     // The filter threshold is computed against the aux range of the tile's group of
     // kGroupTiles consecutive tiles (rows are sorted by aux, so the group range is barely wider

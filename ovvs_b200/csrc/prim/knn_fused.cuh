@@ -139,6 +139,11 @@ struct FusedParams {
   // spans a wide aux range, so the conservative bound lets many columns through to the exact
   // path; computing each value (one FMA per column with aux from shared memory) costs less.
   int exact_filter = 0;
+  // Item table (IVF-Flat list scan): item i = (query pair-tile, first and end database tile),
+  // instead of query pair-tiles x equal super-chunks; num_sc = 1. Query rows ("slots") whose
+  // slot_pair entry is negative are padding and never select.
+  const int4* item_tab = nullptr;
+  const int* slot_pair = nullptr;
   uint64_t* out;                   // [q_pad][num_sc][kListsPerItem][KL] sorted keys (list mode;
                                    // one list per column part)
   int* err;                        // watchdog word

@@ -116,6 +116,18 @@ enum WorkSlot : int {
   kWsIvfSegBegin,
   kWsIvfSegEnd,
   kWsIvfTmp,        // CUB temporary storage
+  kWsIvfTcQueryA,   // tensor-core list scan: fp16 query operand per query, then per slot
+  kWsIvfTcSlotA,
+  kWsIvfTcQueryMul,
+  kWsIvfTcSlotMul,
+  kWsIvfTcQueryNorm,
+  kWsIvfTcFlag,
+  kWsIvfTcCounts,   // slot and item counts and offsets per list
+  kWsIvfTcSlotPair,
+  kWsIvfTcPairSlot,
+  kWsIvfTcItems,
+  kWsIvfTcBound,
+  kWsIvfTcCand,
   kWsCount
 };
 
