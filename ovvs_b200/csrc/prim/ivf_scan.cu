@@ -615,32 +615,25 @@ __global__ void tc_gather_kernel(const uint4* __restrict__ a16_query,
   if (lane == 0) q_mul_slot[s] = pair >= 0 ? q_mul_query[q] : -1.f;
 }
 
-// One warp per (query, probe) pair; kl <= 16, so its 2 * kl candidates fit one per lane.
-__global__ void tc_refine_kernel(const __grid_constant__ IvfScanParams p,
-                                 const uint64_t* __restrict__ tc_cand, int kl,
-                                 const int* __restrict__ pair_slot,
-                                 const int64_t* __restrict__ pos_row) {
-  const int lane = threadIdx.x & 31;
-  const int64_t pair = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (pair >= p.nq * p.nprobe) return;
-  const int64_t q = pair / p.nprobe;
-  const int pr = static_cast<int>(pair % p.nprobe);
-  const int slot = pair_slot[pair];
-  uint64_t key = keys::kEmptyKey;
-  if (slot >= 0 && lane < 2 * kl) {
-    const uint64_t c = tc_cand[static_cast<int64_t>(slot) * 2 * kl + lane];
-    // a list shorter than kl may hold padding positions (ranking value +inf): skipped
-    const int64_t g = c != keys::kEmptyKey ? pos_row[keys::key_id(c)] : -1;
-    if (g >= 0) {
-      const int64_t list = p.probe[pair];
-      const uint32_t concat =
-          p.cum[q * (p.nprobe + 1) + pr] + static_cast<uint32_t>(g - p.list_off[list]);
-      const float v = exact_score(p.metric, p.queries + q * p.dim, p.q_norm[q],
-                                  p.rows + g * p.dim, p.row_norm[g], p.dim);
-      key = keys::make_key(v, concat);
-    }
+// exact_score with the row read four columns at a time (rows 16-byte aligned, dim % 4 == 0);
+// the same operations in the same order.
+template <int ACC>
+__device__ float exact_score_v4(int metric, const float* q, float qn, const float* y, float yn,
+                                int dim) {
+  float acc = 0.f;
+  int cnt = 0;
+  const float4* y4 = reinterpret_cast<const float4*>(y);
+  for (int d4 = 0; d4 < dim / 4; ++d4) {
+    const float4 v = __ldg(y4 + d4);
+    accumulate<ACC>(acc, cnt, q[4 * d4], v.x);
+    accumulate<ACC>(acc, cnt, q[4 * d4 + 1], v.y);
+    accumulate<ACC>(acc, cnt, q[4 * d4 + 2], v.z);
+    accumulate<ACC>(acc, cnt, q[4 * d4 + 3], v.w);
   }
-  // ascending bitonic sort of the 32 keys; lane r keeps the r-th
+  return finish<ACC>(metric, acc, cnt, qn, yn);
+}
+
+__device__ __forceinline__ uint64_t warp_sort_asc(uint64_t key, int lane) {
 #pragma unroll
   for (int size = 2; size <= 32; size <<= 1) {
 #pragma unroll
@@ -651,6 +644,63 @@ __global__ void tc_refine_kernel(const __grid_constant__ IvfScanParams p,
       key = (lower == up) ? (other < key ? other : key) : (other > key ? other : key);
     }
   }
+  return key;
+}
+
+// One warp per (query, probe) pair; kl <= 16, so its 2 * kl candidates fit one per lane. Only
+// the candidates that can reach the pair's exact top k_sel are re-scored: those whose
+// approximate value is within the error margin of the k_sel-th best approximate value (the
+// approximate values v = |y|^2 - 2 q.y are within ~1e-6 of their magnitudes of the exact ones;
+// the margin is 1e-5 of the magnitudes of both values).
+__global__ void tc_refine_kernel(const __grid_constant__ IvfScanParams p,
+                                 const uint64_t* __restrict__ tc_cand, int kl,
+                                 const int* __restrict__ pair_slot,
+                                 const int64_t* __restrict__ pos_row) {
+  const int lane = threadIdx.x & 31;
+  const int64_t pair = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (pair >= p.nq * p.nprobe) return;
+  const int64_t q = pair / p.nprobe;
+  const int pr = static_cast<int>(pair % p.nprobe);
+  const int slot = pair_slot[pair];
+  uint64_t approx = keys::kEmptyKey;
+  int64_t g = -1;
+  if (slot >= 0 && lane < 2 * kl) {
+    approx = tc_cand[static_cast<int64_t>(slot) * 2 * kl + lane];
+    // a list shorter than kl may hold padding positions (ranking value +inf): dropped
+    g = approx != keys::kEmptyKey ? pos_row[keys::key_id(approx)] : -1;
+    if (g < 0) approx = keys::kEmptyKey;
+  }
+  approx = warp_sort_asc(approx, lane);
+  g = approx != keys::kEmptyKey ? pos_row[keys::key_id(approx)] : -1;
+  const float qn = p.q_norm[q];
+  const float yn = g >= 0 ? p.row_norm[g] : 0.f;
+  const float va = keys::key_value(approx);  // NaN for an empty entry
+  const float scale = g >= 0 ? fabsf(va) + qn + yn + 2.f * sqrtf(qn * yn) : 0.f;
+  const float vk = __shfl_sync(0xffffffffu, va, p.k_sel - 1);
+  float smax = lane < p.k_sel ? scale : 0.f;
+#pragma unroll
+  for (int off = 16; off; off >>= 1) smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, off));
+  // rescore when the k_sel-th is empty or not finite, or when within the margin of it
+  const bool rescore = g >= 0 && (lane < p.k_sel || !(fabsf(vk) < __int_as_float(0x7f800000)) ||
+                                  !(va > vk + 1e-5f * (scale + smax)));
+  uint64_t key = keys::kEmptyKey;
+  if (rescore) {
+    const int64_t list = p.probe[pair];
+    const uint32_t concat =
+        p.cum[q * (p.nprobe + 1) + pr] + static_cast<uint32_t>(g - p.list_off[list]);
+    const float* qr = p.queries + q * p.dim;
+    const float* yr = p.rows + g * p.dim;
+    float v;
+    if ((p.dim & 3) == 0) {
+      v = acc_kind(p.metric) == kAccDot
+              ? exact_score_v4<kAccDot>(p.metric, qr, qn, yr, yn, p.dim)
+              : exact_score_v4<kAccL2>(p.metric, qr, qn, yr, yn, p.dim);
+    } else {
+      v = exact_score(p.metric, qr, qn, yr, yn, p.dim);
+    }
+    key = keys::make_key(v, concat);
+  }
+  key = warp_sort_asc(key, lane);
   if (lane < p.k_sel) p.cand[pair * p.k_sel + lane] = key;
 }
 
