@@ -121,8 +121,7 @@ ovvsStatus assign(rt::Resources& r, IvfFlatIndex& ix, const float* d_rows, int64
   return r.finish();
 }
 
-// The list scan of one query block on the tensor cores (ivf_flat.hpp: L2 metrics, no bitset,
-// k <= 10): slots for the block's (query, probe) pairs grouped by list, one fused-kernel item per
+// The list scan of one query block on the tensor cores (ivf_flat.hpp: L2 metrics, k <= 10): slots for the block's (query, probe) pairs grouped by list, one fused-kernel item per
 // (list, 256 slots) over the list's tiles with the exact-value filter, then every pair's
 // candidates re-scored exactly into p.cand (select-mode lists of k for launch_ivf_emit).
 ovvsStatus scan_tc(rt::Resources& r, const IvfFlatIndex& ix, prim::IvfScanParams& p, int64_t k,
@@ -210,6 +209,13 @@ ovvsStatus scan_tc(rt::Resources& r, const IvfFlatIndex& ix, prim::IvfScanParams
     fp.q_bound = bound;
     fp.k_pub = static_cast<int>(k);
     fp.out = cand;
+    if (p.bitset) {  // allow bits by padded position; the re-score also gives filtered rows +inf
+      uint32_t* allow = nullptr;
+      OVVS_TRY(r.scratch(rt::kWsIvfTcAllow, static_cast<size_t>(tc.n_pad / 32), &allow));
+      OVVS_TRY_CUDA(prim::launch_ivf_tc_allow(p.bitset, p.bitset_bits, ix.d_pos_row.as<int64_t>(),
+                                              ix.d_ids.as<int64_t>(), tc.n_pad, allow, s));
+      fp.allow = allow;
+    }
     OVVS_TRY_CUDA(prim::launch_knn_fused(c.maps, fp, kl,
                                          prim::fused_grid(items, nb::pair_sms(r, fp)), s));
   }
@@ -331,8 +337,8 @@ ovvsStatus search_device(rt::Resources& r, const IvfFlatIndex& ix, const float* 
   else
     qb = std::min<int64_t>(qb, std::max<int64_t>(1, (int64_t(1) << 27) / (int64_t(nprobe) * k)));
   const bool coarse_sort = nprobe > prim::kIvfMaxSelect;
-  // the tensor-core scan: L2 metrics, no bitset, k within its 12-entry lists
-  const bool use_tc = ix.tc_ready && d_bitset == nullptr && k <= 10 && !sort_mode;
+  // the tensor-core scan: L2 metrics, k within its 12-entry lists
+  const bool use_tc = ix.tc_ready && k <= 10 && !sort_mode;
 
   float *qn = nullptr, *sc = nullptr, *pval = nullptr;
   int64_t* probe = nullptr;

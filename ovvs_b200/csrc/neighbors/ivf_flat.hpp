@@ -9,7 +9,7 @@
 //            ascending row order.
 //   search:  coarse squared-L2 scores of each query against the centroids (sequential fp32 on
 //            CUDA cores, the reference's prim_pairwise arithmetic) and its nprobe nearest lists;
-//            then the list scan: for the L2 metrics without a bitset and k <= 10 on the tensor
+//            then the list scan: for the L2 metrics and k <= 10 on the tensor
 //            cores (the fused brute-force kernel over (list, 256 probing pairs) items, then an
 //            exact re-score of each pair's candidates: the reference's results except where a
 //            row ties with a pair's k-th within the approximate scores' error, as for the

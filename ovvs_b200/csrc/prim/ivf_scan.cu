@@ -579,6 +579,23 @@ __global__ void tc_counts_kernel(const int* __restrict__ list_q_count,
   item_count[c] = padded / kTcSlots;
 }
 
+// Allow bits by padded position (bit b of word w = position 32 w + b): the bitset bit of the
+// position's original id; padding positions and ids outside the bitset are not allowed.
+__global__ void tc_allow_kernel(const uint8_t* __restrict__ bitset, int64_t bits,
+                                const int64_t* __restrict__ pos_row,
+                                const int64_t* __restrict__ row_ids, int64_t n_pos,
+                                uint32_t* __restrict__ allow_pos) {
+  const int64_t w = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (w * 32 >= n_pos) return;
+  uint32_t word = 0;
+  for (int b = 0; b < 32; ++b) {
+    const int64_t pos = w * 32 + b;
+    const int64_t g = pos < n_pos ? pos_row[pos] : -1;
+    if (g >= 0 && allowed(bitset, bits, row_ids[g])) word |= 1u << b;
+  }
+  allow_pos[w] = word;
+}
+
 // One block per list.
 __global__ void tc_fill_kernel(const int* __restrict__ list_q_count,
                                const int* __restrict__ list_q_off, const int* __restrict__ pair_of,
@@ -691,7 +708,9 @@ __global__ void tc_refine_kernel(const __grid_constant__ IvfScanParams p,
     const float* qr = p.queries + q * p.dim;
     const float* yr = p.rows + g * p.dim;
     float v;
-    if ((p.dim & 3) == 0) {
+    if (p.bitset && !allowed(p.bitset, p.bitset_bits, p.row_ids[g])) {
+      v = __int_as_float(0x7f800000);  // filtered: +inf, ordered by position (indexes.cpp:346-355)
+    } else if ((p.dim & 3) == 0) {
       v = acc_kind(p.metric) == kAccDot
               ? exact_score_v4<kAccDot>(p.metric, qr, qn, yr, yn, p.dim)
               : exact_score_v4<kAccL2>(p.metric, qr, qn, yr, yn, p.dim);
@@ -798,6 +817,16 @@ cudaError_t launch_ivf_tc_counts(const int* list_q_count, const int2* list_tiles
                                  int* slot_count, int* item_count, cudaStream_t stream) {
   tc_counts_kernel<<<static_cast<unsigned>((nlist + 1 + 255) / 256), 256, 0, stream>>>(
       list_q_count, list_tiles, nlist, slot_count, item_count);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ivf_tc_allow(const uint8_t* bitset, int64_t bits, const int64_t* pos_row,
+                                const int64_t* row_ids, int64_t n_pos, uint32_t* allow_pos,
+                                cudaStream_t stream) {
+  const int64_t words = (n_pos + 31) / 32;
+  if (words <= 0) return cudaSuccess;
+  tc_allow_kernel<<<static_cast<unsigned>((words + 255) / 256), 256, 0, stream>>>(
+      bitset, bits, pos_row, row_ids, n_pos, allow_pos);
   return cudaGetLastError();
 }
 

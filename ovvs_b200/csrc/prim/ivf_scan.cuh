@@ -96,7 +96,7 @@ cudaError_t launch_ivf_totals(const uint32_t* cum, int64_t nq, int nprobe, int64
 cudaError_t launch_ivf_seg_bounds(const int64_t* seg_base, const uint32_t* cum, int64_t nq,
                                   int nprobe, int* seg_begin, int* seg_end, cudaStream_t stream);
 
-// ---- tensor-core list scan (L2 family, no bitset, k up to 10) --------------------------------
+// ---- tensor-core list scan (L2 family, k up to 10) --------------------------------------------
 // The (query, probe) pairs of each list get "slots": list c's pairs occupy slots
 // [slot_off[c], slot_off[c] + list_q_count[c]) of a range padded to whole 256-slot pair tiles, and
 // the fused brute-force kernel runs one item per (list, pair tile) over the list's database tiles
@@ -117,6 +117,12 @@ cudaError_t launch_ivf_tc_fill(const int* list_q_count, const int* list_q_off, c
                                const int* slot_off, const int* item_off, const int2* list_tiles,
                                int nlist, int* slot_pair, int* pair_slot, int4* item_tab,
                                cudaStream_t stream);
+
+// Allow bits by padded position for a bitset by original id (allow_pos[w] bit b = position
+// 32 w + b; padding positions are not allowed).
+cudaError_t launch_ivf_tc_allow(const uint8_t* bitset, int64_t bits, const int64_t* pos_row,
+                                const int64_t* row_ids, int64_t n_pos, uint32_t* allow_pos,
+                                cudaStream_t stream);
 
 // The fused kernel's query operand per slot: row s of a16_slot = row (slot_pair[s] / nprobe) of
 // a16_query (zeros for padding slots), row_halves fp16 values each; q_mul_slot likewise (-1 for

@@ -128,6 +128,7 @@ enum WorkSlot : int {
   kWsIvfTcItems,
   kWsIvfTcBound,
   kWsIvfTcCand,
+  kWsIvfTcAllow,
   kWsCount
 };
 

@@ -85,7 +85,9 @@ def _mixture(rng, n, dim, centres, std=2.0):
 
 
 @pytest.mark.parametrize("metric,k,nprobe,with_bits", [
-    ("l2", 10, 8, False),
+    ("l2", 10, 8, False),      # tensor-core scan
+    ("l2", 10, 8, True),       # tensor-core scan with an allow list
+    ("l2", 3, 2, 0.004),       # tensor-core scan, fewer allowed rows than k in most lists
     ("inner_product", 32, 4, True),
     ("cosine", 100, 6, False),
     ("l2", 300, 5, True),      # sort path
@@ -105,7 +107,9 @@ def test_seeded_search_vs_oracle(metric, k, nprobe, with_bits, ovvs, gpu, oracle
     assert np.array_equal(np.sort(parts["ids"]), np.arange(x.shape[0]))
     bits = None
     if with_bits:
-        bits = ovvs.bitset_from_allow_list(x.shape[0], np.nonzero(rng.random(x.shape[0]) < 0.3)[0])
+        frac = 0.3 if with_bits is True else with_bits
+        bits = ovvs.bitset_from_allow_list(x.shape[0],
+                                           np.nonzero(rng.random(x.shape[0]) < frac)[0])
     nb, ds = ix.search(q, k, nprobe, bitset=bits)
     rnb, rds = oracle.ivf_flat_search(x, metric, parts["centroids"], parts["sizes"], parts["ids"],
                                       q, k, nprobe, bits)
