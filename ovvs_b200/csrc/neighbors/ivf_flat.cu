@@ -86,7 +86,19 @@ ovvsStatus assemble(rt::Resources& r, IvfFlatIndex& ix) {
                                                ix.d_rnorm.as<float>(), s));
   }
   OVVS_TRY(r.finish());
-  return assemble_tc(r, ix);
+  // The tensor-core operand is an accelerator: without room for it the CUDA-core scan serves.
+  const ovvsStatus st = assemble_tc(r, ix);
+  if (st == OVVS_STATUS_OOM) {
+    (void)cudaGetLastError();
+    ix.tc_ready = false;
+    for (rt::DeviceBuffer* b : {&ix.tc.rows16, &ix.tc.exact32, &ix.tc.aux, &ix.tc.tile_aux,
+                                &ix.tc.norm_sorted, &ix.tc.row_id, &ix.tc.inv_perm})
+      b->release();
+    ix.d_pos_row.release();
+    ix.d_list_tiles.release();
+    return r.finish();
+  }
+  return st;
 }
 
 // Device centroids, their norms (nrm2sq, sequential) and the assignment index.
