@@ -460,12 +460,24 @@ ovvsStatus search_large(rt::Resources& r, const BruteIndex& ix, const SearchCtx&
 
   prim::FusedParams p;
   OVVS_TRY(base_params(r, ix, c, nq, &p));
-  p.num_sc = choose_num_sc(c.num_qtiles, ix.num_tiles, pair_sms(r, p), 0, &p.tiles_per_item);
-  p.num_items = prim::fused_items(c.num_qtiles, p.num_sc);
   p.q_tau_key = tau;
   p.app_count = count;
   p.app_buf = buf;
   p.app_cap = cap;
+  // The append pass runs in two stages when the bound came from a sample: after the first half
+  // of the tiles each query's bound is tightened to the need-th best key it has appended (about
+  // the 2 x need-th best row instead of the sample's 8 x need-th), so the second half appends
+  // few rows and its epilogue rarely leaves the filter.
+  const bool two_stage = prepass && ix.num_tiles >= 64;
+  const int half = two_stage ? (ix.num_tiles + 1) / 2 : ix.num_tiles;
+  auto stage = [&](int base, int tiles) {
+    prim::FusedParams q = p;
+    q.tile_base = base;
+    q.num_dbtiles = tiles;
+    q.num_sc = choose_num_sc(c.num_qtiles, tiles, pair_sms(r, q), 0, &q.tiles_per_item);
+    q.num_items = prim::fused_items(c.num_qtiles, q.num_sc);
+    return prim::launch_knn_fused(c.maps, q, 0, launch_grid(q, pair_sms(r, q)), s);
+  };
   prim::SelectParams sp{};
   sp.m = m;
   sp.count = count;
@@ -479,7 +491,11 @@ ovvsStatus search_large(rt::Resources& r, const BruteIndex& ix, const SearchCtx&
     p.app_exact = round >= 2;  // persistent overflow: strict key bound (ties cannot pile up)
     OVVS_TRY_CUDA(cudaMemsetAsync(count, 0, static_cast<size_t>(c.q_pad) * sizeof(uint32_t), s));
     OVVS_TRY_CUDA(cudaMemsetAsync(overflow, 0, sizeof(int), s));
-    OVVS_TRY_CUDA(prim::launch_knn_fused(c.maps, p, 0, launch_grid(p, pair_sms(r, p)), s));
+    OVVS_TRY_CUDA(stage(0, half));
+    if (two_stage) {
+      OVVS_TRY_CUDA(prim::launch_tighten_tau(buf, count, cap, nq, static_cast<int>(need), tau, s));
+      OVVS_TRY_CUDA(stage(half, ix.num_tiles - half));
+    }
     OVVS_TRY_CUDA(prim::launch_select_rerank(sp, s));
     int host_overflow = 0;
     OVVS_TRY_CUDA(cudaMemcpyAsync(&host_overflow, overflow, sizeof(int), cudaMemcpyDeviceToHost, s));

@@ -81,8 +81,8 @@ __device__ __forceinline__ Item item_of(const FusedParams& p, int item, uint32_t
   const int qp = item % num_qpairs;
   it.qt = 2 * qp + static_cast<int>(rank);
   it.sc = item / num_qpairs;
-  it.t0 = it.sc * p.tiles_per_item;
-  it.t1 = min(it.t0 + p.tiles_per_item, p.num_dbtiles);
+  it.t0 = p.tile_base + it.sc * p.tiles_per_item;
+  it.t1 = min(it.t0 + p.tiles_per_item, p.tile_base + p.num_dbtiles);
   return it;
 }
 __device__ __forceinline__ int first_item() { return static_cast<int>(blockIdx.x >> 1); }

@@ -148,6 +148,8 @@ struct FusedParams {
                                    // one list per column part)
   int* err;                        // watchdog word
   int tile_stride = 1;             // item tile ranges count every tile_stride-th database tile
+  int tile_base = 0;               // first database tile of this launch (the launch covers tiles
+                                   // [tile_base, tile_base + num_dbtiles))
   // Append mode (KL = 0): every column whose key is within the query's bound q_tau_key[q] is
   // appended to the query's buffer app_buf[q * app_cap + i]; app_count[q] counts them (it may
   // exceed app_cap: the caller then tightens the bound and runs again). With a finite bound value

@@ -388,6 +388,40 @@ __global__ void kth_bound_kernel(const uint64_t* __restrict__ cand, int num_sc, 
   if (lane == 0) tau_key[q] = kth;
 }
 
+// Large k, between the stages of the append pass: the need-th smallest key among the keys a
+// query has appended so far bounds its need-th best key overall (they are real rows), so it
+// replaces tau_key[q] when smaller. Each lane keeps the 4 smallest keys of its strided share and
+// the warp takes the need-th smallest of those 128: the need-th smallest of a subset is never
+// below the set's, so the result stays a valid bound (a little looser when a lane held more
+// than 4 of the set's smallest need).
+__global__ void tighten_tau_kernel(const uint64_t* __restrict__ app_buf,
+                                   const uint32_t* __restrict__ app_count, int cap, int64_t nq,
+                                   int need, uint64_t* __restrict__ tau_key) {
+  const int lane = threadIdx.x & 31;
+  const int64_t q = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (q >= nq) return;
+  const int count = static_cast<int>(min(app_count[q], static_cast<uint32_t>(cap)));
+  if (count < need) return;  // too few so far to bound rank `need`
+  const uint64_t* b = app_buf + static_cast<size_t>(q) * cap;
+  uint64_t L[4] = {kEmptyKey, kEmptyKey, kEmptyKey, kEmptyKey};
+  for (int i = lane; i < count; i += 32) {
+    const uint64_t key = b[i];
+    if (key < L[3]) list_insert<4>(L, key);
+  }
+  int ptr = 0;
+  uint64_t kth = kEmptyKey;
+  for (int r = 0; r < need; ++r) {
+    uint64_t head = ptr == 0 ? L[0] : ptr == 1 ? L[1] : ptr == 2 ? L[2] : ptr == 3 ? L[3]
+                                                                           : kEmptyKey;
+    int bl = lane;
+    warp_argmin(head, bl);
+    if (head == kEmptyKey) return;  // fewer than `need` keys held: no bound
+    if (lane == bl) ++ptr;
+    kth = head;
+  }
+  if (lane == 0 && kth < tau_key[q]) tau_key[q] = kth;
+}
+
 __device__ __forceinline__ void bitonic_block(uint64_t* key, float* val, int n) {
   // Ascending bitonic sort of n (power of two) entries in shared memory by the whole block.
   for (int size = 2; size <= n; size <<= 1) {
@@ -514,6 +548,15 @@ cudaError_t launch_kth_bound(const uint64_t* cand, int num_sc, int64_t nq, int k
   const int64_t blocks = (nq + wpb - 1) / wpb;
   kth_bound_kernel<<<static_cast<unsigned>(blocks), wpb * 32, 0, stream>>>(cand, num_sc, nq, k,
                                                                         kl, tau_key);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tighten_tau(const uint64_t* app_buf, const uint32_t* app_count, int cap,
+                              int64_t nq, int need, uint64_t* tau_key, cudaStream_t stream) {
+  if (need < 1 || nq <= 0) return cudaSuccess;
+  const int wpb = 8;
+  tighten_tau_kernel<<<static_cast<unsigned>((nq + wpb - 1) / wpb), wpb * 32, 0, stream>>>(
+      app_buf, app_count, cap, nq, need, tau_key);
   return cudaGetLastError();
 }
 

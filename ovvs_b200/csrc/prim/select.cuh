@@ -50,6 +50,12 @@ cudaError_t launch_merge_rerank(const MergeParams& p, cudaStream_t stream);
 // Large k. tau_key[q] = the k-th smallest key of the union of the num_sc sorted lists of kl keys
 // in cand (kEmptyKey when the union has fewer than k keys): an upper bound on the k-th best key
 // of the whole database, since the union holds real rows.
+// Large k, between stages of the append pass: tau_key[q] = min(tau_key[q], an upper bound on the
+// need-th smallest key among the min(app_count[q], cap) keys appended so far), for queries that
+// appended at least `need` keys.
+cudaError_t launch_tighten_tau(const uint64_t* app_buf, const uint32_t* app_count, int cap,
+                              int64_t nq, int need, uint64_t* tau_key, cudaStream_t stream);
+
 cudaError_t launch_kth_bound(const uint64_t* cand, int num_sc, int64_t nq, int k, int kl,
                              uint64_t* tau_key, cudaStream_t stream);
 
