@@ -123,3 +123,21 @@ def test_parity_flags_mismatches_beyond_ties():
     # same ids with different distance bits fail
     p = bench._parity(nb_ref, np.array([[1.0, 2.0, 3.0000002]], np.float32), nb_ref, ds_ref, 1e-4)
     assert not p["ok"] and p["distance_bits_differ_where_ids_agree"] == 1
+
+
+def test_primitive_configs():
+    """The dense-primitive arms: seeded operands of the configured shapes, a named metric, and a
+    reference sample sized to the requested seconds of the reference's single-threaded loop."""
+    for name in ("pw", "gemm"):
+        cfg = bench.CONFIGS[name]
+        x, y = bench._prim_data(cfg)
+        assert x.shape == (cfg["nx"], cfg["dim"]) and y.shape == (cfg["ny"], cfg["dim"])
+        assert x.dtype == np.float32 and y.dtype == np.float32
+        x2, _ = bench._prim_data(cfg)
+        assert np.array_equal(x, x2)  # seeded
+        assert cfg["op"] in bench._prim_metric(cfg)
+        rows = bench._prim_reference_rows(cfg, 12.0)
+        assert 1 <= rows <= cfg["nx"]
+        # about 12 s at the reference's measured ~2.1 GFLOP/s
+        assert abs(2.0 * rows * cfg["ny"] * cfg["dim"] / 2.1e9 - 12.0) < 1.0
+        assert bench._prim_reference_rows(cfg, 1e9) == cfg["nx"]
