@@ -77,7 +77,9 @@ OVVS_API ovvsStatus ovvsWatchdogSelfTest(ovvsResources_t res, int64_t limit_ns, 
 
 /* Same contract as ovvsBruteForceSearch, but queries, bitset, neighbors and distances are device
    pointers on the Resources' device, and the call only enqueues work on the Resources' stream
-   (no host synchronisation). Output rows have stride min(k, n). Call ovvsResourcesSynchronize
+   (no host synchronisation), except for k above the register lists (k beyond 28), where it waits
+   for its own work once per pass to check the candidate buffers for overflow. Output rows have
+   stride min(k, n). Call ovvsResourcesSynchronize
    (or synchronise the stream) before reading the results. On a sharded Resources the call is
    collective: every rank passes the same queries and receives the global result. */
 OVVS_API ovvsStatus ovvsBruteForceSearchDevice(ovvsResources_t res, ovvsBruteForceIndex_t index,
@@ -113,8 +115,10 @@ OVVS_API ovvsStatus ovvsBruteForceSearchDeviceNoAlloc(ovvsResources_t res,
 /* Device-pointer IVF-Flat search: the contract of ovvsIvfFlatSearch (reference
    src/neighbors/indexes.cpp:302-358; outputs [nq x k], -1 / +inf past a query's candidates) with
    queries, bitset (indexed by row id, covering the index's rows), neighbors and distances in GPU
-   memory on the Resources' device. Only enqueues work on the Resources' stream; synchronise
-   before reading the results. Not in the reference. */
+   memory on the Resources' device. Enqueues work on the Resources' stream; synchronise before
+   reading the results. With the L2 metrics and k <= 10 (the tensor-core list scan) the call also
+   waits once per query block for the stream's work so far, to size the scan's work items from
+   the probe counts. Not in the reference. */
 OVVS_API ovvsStatus ovvsIvfFlatSearchDevice(ovvsResources_t res, ovvsIvfFlatIndex_t index,
                                             const float* d_queries, int64_t nq, int64_t k,
                                             int32_t nprobe, const uint8_t* d_bitset,
